@@ -1,0 +1,397 @@
+"""Benchmark of the MiniCPM5 prefill-score path on B200 (one process per GPU, independent replicas).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mk|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+
+Workload (BASELINE metric "prefill tok/s (MiniCPM5-1B 32x8192, 1/2/4/8 B200); p50 ms at 1x8192"):
+MiniCPM5-1B primary config (24 layers, H 1536, 16Q/2KV, head_dim 96, I 4608, vocab 73448, muP),
+random-init weights, int8 weight-only linears, bf16 activations, a global batch of 32 sequences x
+8192 synthetic token ids (uniform in [1000, 30000), seed 1234, a fresh draw per step) sharded
+evenly over the N ranks (each rank holds a full weight replica; no collective on the data path).
+One step = one prefill-score forward of the rank's sequences returning one greedy token each.
+
+value  : whole-job tokens/s, ids already resident in HBM, device-timed with CUDA events, max over
+         ranks.  Every step's working set (weights + activations) is far larger than L2.
+e2e    : the same through MkEngine.forward with the ids copied from pinned host memory each step
+         and the greedy ids read back to the host each step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "minicpm5-vllm-tpu_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "prefill tok/s (MiniCPM5-1B 32x8192, 1/2/4/8 B200); p50 ms at 1x8192"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mk", choices=["mk", "reference"])
+    ap.add_argument("--config", default="minicpm5-1b")
+    ap.add_argument("--global-bs", type=int, default=32)
+    ap.add_argument("--seq", type=int, default=8192)
+    ap.add_argument("--latency-runs", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def _flops_per_seq(cfg, S):
+    """Skip-aware algorithmic FLOPs of one S-token prefill-score (layers 0..L-2 in full, layer L-1 as
+    K/V projection for every position + Q/O/MLP/attention for the last token, last-token lm_head).
+    Same terms as the reference's verify formula (benchmark/verify_results.py:131-140)."""
+    H, I, L, hd, nq, nkv, V = cfg.hidden, cfg.inter, cfg.num_layers, cfg.head_dim, cfg.n_q, cfg.n_kv, cfg.vocab
+    lin_tok = 2 * (H * (nq + 2 * nkv) * hd + nq * hd * H + 2 * H * I + I * H)
+    attn_seq = 2 * S * S * hd * nq  # causal: (QK^T + PV) halved
+    full = (L - 1) * (S * lin_tok + attn_seq)
+    last = 2 * S * H * 2 * nkv * hd + lin_tok - 2 * H * 2 * nkv * hd + 4 * S * hd * nq
+    head = 2 * H * V
+    return full + last + head
+
+
+def _clock_sampler(gpu_index):
+    try:
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        return subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def _clock_summary(proc):
+    if proc is None:
+        return None
+    proc.terminate()
+    try:
+        out, _ = proc.communicate(timeout=5)
+    except Exception:  # noqa: BLE001
+        proc.kill()
+        return None
+    sm, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in out.strip().splitlines():
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx = float(f[2])
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower().startswith("active"):
+                reasons.add(n)
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _traffic_per_launch(kernel):
+    """dram bytes per launch of `kernel` at the bench workload, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith(kernel + ":"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_sample(cfg, S, target_s, threads):
+    """Time the CPU FP32 oracle (restatement of the reference's f32_golden path) on a bounded sample:
+    decoder layers of one S-token sequence run one at a time until ~target_s of CPU time, then
+    extrapolated to the full model.  Returns (tok/s, sample description)."""
+    from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
+    from oracle import golden
+
+    torch.set_num_threads(threads)
+    c1 = cfg.replace(num_layers=1, vocab=min(cfg.vocab, 4096))
+    sd = random_state_dict(c1, seed=1234)
+    W = golden.golden_weights(sd, c1)
+    ids = synthetic_ids(1, S, seed=1234, vocab=c1.vocab)[0]
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        golden.forward_logits(ids, W, c1, last_only=False)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start >= target_s or len(times) >= cfg.num_layers:
+            break
+    per_layer = statistics.median(times)
+    total = per_layer * cfg.num_layers
+    return S / total, (f"1 x {S} tokens through {len(times)} full decoder layer(s) of the FP32 oracle "
+                       f"(median {per_layer:.2f} s/layer), extrapolated x{cfg.num_layers} layers")
+
+
+def run_reference(a, rank, world):
+    """--impl reference: the reference's CPU FP32 path (oracle port of benchmark/f32_golden.py) on the
+    host cores; rank 0 only."""
+    if rank != 0:
+        return
+    from minicpm5_mk.mk_config import get_config
+
+    cfg = get_config(a.config)
+    threads = os.cpu_count() or 1
+    vals = []
+    desc = ""
+    for i in range(a.warmup + a.steps):
+        v, desc = cpu_sample(cfg, a.seq, target_s=0.0, threads=threads)  # one layer per step
+        if i >= a.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(a.seq / value * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{a.config} 1x{a.seq} prefill-score, CPU FP32 oracle (one layer per step, "
+                                   f"extrapolated)", "seq_len": a.seq, "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = _args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from minicpm5_mk import mk_weights, ops
+    from minicpm5_mk.mk_config import get_config
+    from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
+
+    cfg = get_config(a.config).replace(max_seq=max(a.seq, 8192))
+    if a.global_bs % world:
+        raise SystemExit(f"global batch {a.global_bs} not divisible by {world} ranks")
+    bs = a.global_bs // world
+    S = a.seq
+    T = bs * S
+
+    # Full weight replica on this GPU (random-init from the device generator, prepared on device).
+    sd = random_state_dict(cfg, seed=1234, device=dev)
+    pw = mk_weights.prepare_mk_weights(sd, cfg)
+    del sd
+    torch.cuda.empty_cache()
+    eng = ops.MkEngine(cfg, pw, dev)
+    del pw
+
+    nbat = a.warmup + a.steps
+    ids_host = [synthetic_ids(bs, S, seed=1234 + 1000 * rank + i).reshape(-1).contiguous().pin_memory()
+                for i in range(nbat)]
+    ids_dev = [t.to(dev) for t in ids_host]
+    hid = torch.empty((bs, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    lg = torch.empty((bs, cfg.vocab), dtype=torch.float32, device=dev)
+    top1 = torch.empty((bs,), dtype=torch.int32, device=dev)
+    out = (hid, lg, top1)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------------------- device-timed throughput
+    for i in range(a.warmup):
+        eng.forward(ids_dev[i], bs, S, out=out)
+    torch.cuda.synchronize()
+    eng.check_device_error()
+    clk = _clock_sampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(a.steps):
+        eng.forward(ids_dev[a.warmup + i], bs, S, out=out)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = _clock_summary(clk)
+    dev_ms = ev0.elapsed_time(ev1) / a.steps
+    step_ms = max_over_ranks(dev_ms)
+    err = eng.check_device_error()
+    total_tokens = a.global_bs * S
+    value = total_tokens / (step_ms / 1e3)
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    e2e = None
+    if not a.no_e2e:
+        ids_buf = torch.empty((T,), dtype=torch.int32, device=dev)
+        top1_host = torch.empty((bs,), dtype=torch.int32).pin_memory()
+        for i in range(min(2, a.warmup)):
+            ids_buf.copy_(ids_host[i], non_blocking=True)
+            eng.forward(ids_buf, bs, S, out=out)
+            top1_host.copy_(top1, non_blocking=True)
+            stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(a.steps):
+            ids_buf.copy_(ids_host[a.warmup + i], non_blocking=True)
+            eng.forward(ids_buf, bs, S, out=out)
+            top1_host.copy_(top1, non_blocking=True)
+            stream.synchronize()
+            _ = top1_host.tolist()  # the host reads each step's result
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - t0) * 1e3 / a.steps
+        e2e_ms = max_over_ranks(max(wall_ms, e0.elapsed_time(e1) / a.steps))
+        e2e = {"value": round(total_tokens / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(e2e_ms, 3),
+               "h2d_bytes_per_step": int(T * 4) * world, "d2h_bytes_per_step": int(bs * 4) * world,
+               "api": "minicpm5_mk.ops.MkEngine.forward -> mk_forward (C ABI)"}
+
+    # ---------------------------------------------------------------- latency at 1 x 8192
+    lat = None
+    if rank == 0 and a.latency_runs > 0:
+        one = ids_dev[0][:S].contiguous()
+        o1 = (hid[:1], lg[:1], top1[:1])
+        for _ in range(5):
+            eng.forward(one, 1, S, out=o1)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(a.latency_runs):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            eng.forward(one, 1, S, out=o1)
+            s1.record(stream)
+            s1.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        ts.sort()
+
+        def pct(p):
+            k = (len(ts) - 1) * p / 100.0
+            lo = int(k)
+            hi = min(lo + 1, len(ts) - 1)
+            return ts[lo] + (ts[hi] - ts[lo]) * (k - lo)
+
+        lat = {"p50_ms": round(pct(50), 3), "p99_ms": round(pct(99), 3), "runs": len(ts), "warmup": 5,
+               "timing": "device (CUDA events)"}
+    barrier()
+
+    # ---------------------------------------------------------------- roofline of the dominant kernels
+    peaks, peak_kind = _peaks()
+    kern = {}
+    if rank == 0:
+        g = torch.Generator(device=dev).manual_seed(5)
+        x = (torch.randn((T, cfg.hidden), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        rstd = torch.ones((T,), device=dev)
+        w_gu, s_gu = eng.weights["w_gu"][0], eng.weights["s_gu"][0]
+        hbuf = torch.empty((T, cfg.inter), dtype=torch.bfloat16, device=dev)
+        qkv = (torch.randn((T, cfg.qkv_dim), generator=g, device=dev)).to(torch.bfloat16)
+        abuf = torch.empty((T, cfg.q_dim), dtype=torch.bfloat16, device=dev)
+
+        def timeit(fn, n=3):
+            fn()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(n):
+                fn()
+            s1.record(stream)
+            s1.synchronize()
+            return s0.elapsed_time(s1) / n
+
+        from minicpm5_mk import _lib
+        ms_gu = timeit(lambda: ops.gemm_w8a16(x, w_gu, s_gu, _lib.MK_GEMM_SWIGLU, row_scale=rstd, out=hbuf))
+        ms_at = timeit(lambda: ops.attention_prefill(qkv, bs, S, cfg.n_q, cfg.n_kv, cfg.head_dim, out=abuf))
+        fl_gu = 2.0 * T * cfg.hidden * 2 * cfg.inter
+        fl_at = 2.0 * S * S * cfg.head_dim * cfg.n_q * bs
+        n_layers = cfg.num_layers - 1
+        kern = {
+            "gemm_w8a16_swiglu": {"ms": ms_gu, "tflops": fl_gu / ms_gu / 1e9, "flops": fl_gu,
+                                  "share": ms_gu * n_layers / dev_ms},
+            "attn_prefill": {"ms": ms_at, "tflops": fl_at / ms_at / 1e9, "flops": fl_at,
+                             "share": ms_at * n_layers / dev_ms},
+        }
+        del x, hbuf, qkv, abuf
+    dom = max(kern, key=lambda k: kern[k]["share"]) if kern else None
+    roofline = None
+    if dom:
+        k = kern[dom]
+        peak = peaks["bf16_tflops"]
+        tr = _traffic_per_launch(dom)
+        roofline = {"kernel": dom, "bound": "tensor", "achieved": round(k["tflops"], 1), "peak": peak,
+                    "unit": "TFLOP/s", "frac": round(k["tflops"] / peak, 4), "peak_kind": f"{peak_kind} (burst)",
+                    "traffic": tr, "flops_per_launch": k["flops"], "ms_per_launch": round(k["ms"], 4),
+                    "share_of_step": round(k["share"], 3),
+                    "others": {n: {"achieved": round(v["tflops"], 1), "frac": round(v["tflops"] / peak, 4),
+                                   "ms_per_launch": round(v["ms"], 4), "share_of_step": round(v["share"], 3)}
+                               for n, v in kern.items() if n != dom}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, desc = cpu_sample(cfg, S, a.cpu_seconds, threads)
+        cpu = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+
+    fl_step = _flops_per_seq(cfg, S) * a.global_bs
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{a.config} prefill-score {a.global_bs}x{S} (1 greedy token per sequence), "
+                              f"int8 weight-only linears, bf16 activations",
+                   "model": a.config, "global_batch": a.global_bs, "seq_len": S, "per_gpu_batch": bs,
+                   "parallelism": f"dp{world} (independent full replicas, no collective)",
+                   "l2": "working set (0.9 GB weights + activations) larger than L2 every step"},
+        "model_tflops": round(fl_step / (step_ms / 1e3) / 1e12, 1),
+        "model_roofline_frac": round(fl_step / (step_ms / 1e3) / 1e12 / (peaks["bf16_tflops"] * world), 4),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": eng.launches_per_forward(bs, S) * a.steps,
+        "clocks": clocks, "latency_1x8192": lat, "device_error": err,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

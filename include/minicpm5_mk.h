@@ -1,0 +1,171 @@
+/*
+ * minicpm5_mk -- C ABI of the B200 (sm_100a) MiniCPM5 prefill-score path.
+ *
+ * The reference reaches its device program through one op,
+ *   jax_op("minicpm5_mk::forward", mk_jax.mk_forward)          plugin/minicpm5_mk/model.py:57-66
+ * called from MiniCPM5MegakernelForCausalLM._mk_call            plugin/minicpm5_mk/model.py:737-753
+ * with (ids, embed, cos, sin, final_norm, 16 weight stacks, bs, seq, quant, n_q, n_kv, head_dim,
+ * eps, attn) and returning (max(8, bs), H) bf16 final-normed last-token hidden rows
+ * (plugin/minicpm5_mk/mk_jax.py:624-665).  This library replaces that op.  The weights are bound
+ * once (mk_bind_weights, the counterpart of the `_mk_build` device copy, model.py:623-698) and
+ * each forward passes only the ids, a caller-owned workspace and the outputs.
+ *
+ * Conventions
+ *   - Plain C types only; every device buffer is owned by the caller (e.g. the torch caching
+ *     allocator).  The library owns the handle and its host-side descriptors.
+ *   - No exceptions cross the ABI: every call returns an mk_status.
+ *   - All launches are asynchronous on the given stream; no call synchronises the host except
+ *     mk_get_error (which reads the device error word).
+ *   - One handle per device; calls on one handle are serialised by the caller.
+ *   - bf16 = IEEE bfloat16 stored as uint16_t; "stream" is a cudaStream_t passed as void*.
+ */
+#ifndef MINICPM5_MK_H_
+#define MINICPM5_MK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mk_status {
+  MK_OK = 0,
+  MK_ERR_BAD_SHAPE = 1,      /* unsupported or inconsistent sizes (e.g. seq % 128, head_dim not 96/128) */
+  MK_ERR_BAD_ALIGN = 2,      /* a pointer is not 16-byte aligned */
+  MK_ERR_CUDA = 3,           /* a CUDA runtime / driver call failed */
+  MK_ERR_DEVICE_TIMEOUT = 4, /* a kernel gave up a bounded wait (see mk_get_error) */
+  MK_ERR_BAD_ARG = 5,        /* null handle / pointer, bad enum value */
+  MK_ERR_NOT_BOUND = 6,      /* mk_forward before mk_bind_weights */
+  MK_ERR_BAD_TOKEN = 7,      /* a token id outside [0, vocab) was seen */
+  MK_ERR_WORKSPACE = 8       /* workspace smaller than mk_workspace_size */
+} mk_status;
+
+/* Model configuration: plugin/minicpm5_mk/model.py:561-567 plus the MiniCPM muP scalars.
+ *   x = scale_emb * embed[ids];  x += residual_scale * branch;  logits = logit_scale * h @ lm_head^T */
+typedef struct mk_config {
+  int32_t num_layers, hidden, inter, n_q, n_kv, head_dim, vocab, max_seq;
+  float eps, rope_theta, scale_emb, residual_scale, logit_scale;
+} mk_config;
+
+/* Device pointers of the prepared weights (layout written by minicpm5_mk/mk_weights.py):
+ *   embed, lm_head : bf16 [vocab, hidden]
+ *   final_norm     : f32  [hidden]
+ *   rope_cos/sin   : f32  [max_seq, head_dim/2]
+ *   w_qkv  int8 [L, (n_q+2 n_kv) head_dim, hidden]   s_qkv  f32 [L, (n_q+2 n_kv) head_dim]
+ *   w_o    int8 [L, hidden, n_q head_dim]            s_o    f32 [L, hidden]
+ *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows interleaved in blocks of 128)
+ *                                                    s_gu   f32 [L, 2 inter]
+ *   w_down int8 [L, hidden, inter]                   s_down f32 [L, hidden]
+ * The Q rows carry 1/sqrt(head_dim); RMSNorm gains are folded into the weight columns. */
+typedef struct mk_weight_ptrs {
+  const void* embed;
+  const void* lm_head;
+  const float* final_norm;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int8_t* w_qkv;
+  const float* s_qkv;
+  const int8_t* w_o;
+  const float* s_o;
+  const int8_t* w_gu;
+  const float* s_gu;
+  const int8_t* w_down;
+  const float* s_down;
+} mk_weight_ptrs;
+
+typedef struct mk_handle mk_handle;
+
+/* Human-readable name of a status code (static string). */
+const char* mk_status_string(mk_status s);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int32_t mk_version(void);
+
+/* Create a handle on `device` (the CUDA device ordinal).  Replaces the op creation in
+ * plugin/minicpm5_mk/model.py:57-66 (`_get_op`). */
+mk_status mk_create(const mk_config* cfg, int32_t device, mk_handle** out);
+
+/* Bind the prepared weights (device pointers stay owned by the caller and must outlive the
+ * handle's use).  Builds the TMA descriptors of the weight stacks.  Counterpart of the device
+ * copy in `_mk_build` (plugin/minicpm5_mk/model.py:623-698). */
+mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w);
+
+/* Bytes of workspace mk_forward needs for (bs, seq). */
+mk_status mk_workspace_size(const mk_handle* h, int32_t bs, int32_t seq, size_t* bytes);
+
+/* Whole-model prefill-score forward of `bs` equal-length sequences of length `seq`
+ * (replaces mk_forward, plugin/minicpm5_mk/mk_jax.py:624-665, and vLLM's lm_head + greedy sampler
+ * for those rows).
+ *   d_ids       int32 [bs * seq], sequence-major
+ *   d_workspace >= mk_workspace_size bytes, 256-byte aligned
+ *   d_hidden    optional bf16 [bs, hidden]: final-normed last-token hidden rows (the reference op's output)
+ *   d_logits    optional f32 [bs, vocab]: last-token logits (logit_scale applied)
+ *   d_top1      optional int32 [bs]: greedy token (argmax of the logits, ties -> lowest id)
+ * seq must be a multiple of 128 and <= max_seq; bs >= 1. */
+mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                     size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream);
+
+/* Number of kernel launches one mk_forward(bs, seq) issues (for launch accounting). */
+int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq);
+
+/* Read and clear the library's device error word (synchronises the device).  *device_err
+ * receives the raw code (0 = none); the return value maps it to an mk_status. */
+mk_status mk_get_error(mk_handle* h, int32_t* device_err);
+
+void mk_destroy(mk_handle* h);
+
+/* ---------------------------------------------------------------- isolated kernels
+ * The per-stage kernels of the forward, exposed for parity tests and the isolated-kernel
+ * benchmarks.  They use the current device and build their descriptors per call. */
+
+/* GEMM epilogue modes. */
+typedef enum mk_gemm_mode {
+  MK_GEMM_ROWSCALE = 0, /* out = bf16(acc * row_scale[m] * col_scale[n])                     */
+  MK_GEMM_RESID = 1,    /* out = bf16(out + resid_scale * acc * col_scale[n])   (in place)   */
+  MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g) * u) over 128-row gate/up blocks; out width N/2 */
+  MK_GEMM_COLSCALE = 3  /* out = bf16(acc * col_scale[n])                                    */
+} mk_gemm_mode;
+
+/* W8A16 GEMM: acc[m, n] = sum_k a[m, k] * w[n, k]; a bf16 [M, lda], w int8 [N, K].
+ * N % 128 == 0 (N % 256 == 0 for SWIGLU), K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
+ * Replaces `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` (mk_jax.py:233-269) and the
+ * gate/up half of `fused_mlp` (mk_mlp.py:68-145). */
+mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
+                        int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
+                        void* stream);
+
+/* Causal GQA prefill attention over bs sequences of length seq.  qkv bf16 [bs*seq, ld_qkv] with
+ * Q heads at column q_col, K at k_col, V at v_col (each head head_dim wide); out bf16
+ * [bs*seq, ld_out] (head h at column h*head_dim).  Scores are multiplied by `softmax_scale`
+ * (1.0 when Q already carries 1/sqrt(head_dim)).  n_q / n_kv must be 1, 2, 4 or 8.
+ * Replaces `super_gqa_v2` (plugin/minicpm5_mk/mk_attn.py:557-710). */
+mk_status mk_attention_prefill(const void* qkv, int32_t bs, int32_t seq, int32_t n_q, int32_t n_kv,
+                               int32_t head_dim, int32_t ld_qkv, int32_t q_col, int32_t k_col, int32_t v_col,
+                               float softmax_scale, void* out, int32_t ld_out, void* stream);
+
+/* In-place RoPE on n_heads heads starting at column col0 of each of `rows` rows (row r at position
+ * pos_base + r % seq).  Tables f32 [*, head_dim/2].  (RoPE of plugin/minicpm5_mk/mk_attn.py:572-589,
+ * math of benchmark/f32_golden.py:57-59,88-89.) */
+mk_status mk_rope(void* x, int32_t rows, int32_t ld, int32_t col0, int32_t n_heads, int32_t head_dim,
+                  const float* rope_cos, const float* rope_sin, int32_t seq, int32_t pos_base, void* stream);
+
+/* rstd[t] = 1/sqrt(mean(x[t, :H]^2) + eps)  (`rms_norm_unit`, plugin/minicpm5_mk/mk_jax.py:32-36). */
+mk_status mk_rms_rstd(const void* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream);
+
+/* x[t] = bf16(scale * embed[ids[t]])  (plugin/minicpm5_mk/mk_jax.py:532). */
+mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, void* x,
+                   void* stream);
+
+/* logits[b] = h[b] @ lm_head^T (f32), top1[b] = argmax (ties -> lowest id) for h f32 [bs, H].
+ * part_val/part_idx: scratch of bs * mk_lm_head_parts() entries each.
+ * (vLLM LogitsProcessor + greedy sampler after the reference op.) */
+int32_t mk_lm_head_parts(void);
+mk_status mk_lm_head_argmax(const float* h, int32_t bs, int32_t H, const void* lm_head, int32_t V, float* logits,
+                            float* part_val, int32_t* part_idx, int32_t* top1, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINICPM5_MK_H_ */

@@ -1,0 +1,542 @@
+// C ABI of the minicpm5_mk B200 library: handle / weight binding / whole-model forward
+// orchestration, plus the isolated per-stage entry points.  See include/minicpm5_mk.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/minicpm5_mk.h"
+#include "mk_attn.cuh"
+#include "mk_common.cuh"
+#include "mk_gemm.cuh"
+#include "mk_small.cuh"
+
+namespace {
+
+using mk::AttnArgs;
+using mk::AttnLastArgs;
+using mk::GemmArgs;
+
+// Library device error word (one per device that loads the library); first error wins.
+__device__ int g_mk_err;
+
+constexpr int kMaxDevices = 64;
+constexpr int kLmParts = 296;
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+  int* err = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_encodeTiled g_encode = nullptr;
+
+mk_status cuda_status(cudaError_t e) { return e == cudaSuccess ? MK_OK : MK_ERR_CUDA; }
+
+#define MK_CUDA(x)                                   \
+  do {                                               \
+    cudaError_t e_ = (x);                            \
+    if (e_ != cudaSuccess) return MK_ERR_CUDA;       \
+  } while (0)
+#define MK_TRY(x)                \
+  do {                           \
+    mk_status s_ = (x);          \
+    if (s_ != MK_OK) return s_;  \
+  } while (0)
+
+// Per-device one-time set-up: SM count, error-word address, kernel attributes, driver entry point.
+mk_status device_state(DeviceState** out) {
+  int dev = 0;
+  MK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return MK_ERR_BAD_ARG;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    MK_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev));
+    void* p = nullptr;
+    MK_CUDA(cudaGetSymbolAddress(&p, g_mk_err));
+    d.err = static_cast<int*>(p);
+    MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::G_SMEM_BYTES)));
+    MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::AttnShape<96>::SMEM)));
+    MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::AttnShape<128>::SMEM)));
+    MK_CUDA(cudaFuncSetAttribute(mk::attn_last_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+    MK_CUDA(cudaFuncSetAttribute(mk::lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      MK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+      if (q != cudaDriverEntryPointSuccess || !fn) return MK_ERR_CUDA;
+      g_encode = reinterpret_cast<PFN_encodeTiled>(fn);
+    }
+    d.ready = true;
+  }
+  *out = &d;
+  return MK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// A operand: bf16 [rows, ld], box 64 (K) x 128 (rows), 128-byte swizzle.
+mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GM)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
+}
+
+// B operand: int8 [N, K] (K contiguous), box 64 (K) x 256 (N), no swizzle.
+mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GN)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
+}
+
+mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
+                      int mode, const float* row_scale, const float* col_scale, void* out, int ldo, float resid,
+                      cudaStream_t st) {
+  GemmArgs ga;
+  ga.M = M;
+  ga.N = N;
+  ga.K = K;
+  ga.mode = mode;
+  ga.row_scale = row_scale;
+  ga.col_scale = col_scale;
+  ga.out = static_cast<__nv_bfloat16*>(out);
+  ga.ldo = ldo;
+  ga.resid_scale = resid;
+  ga.err = d->err;
+  const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
+  const int grid = std::max(1, std::min(tiles, d->sm_count));
+  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+  return cuda_status(cudaGetLastError());
+}
+
+mk_status check_gemm_shape(int M, int N, int K, int mode) {
+  if (M <= 0 || N <= 0 || K <= 0) return MK_ERR_BAD_SHAPE;
+  if (N % 128 || K % mk::GK) return MK_ERR_BAD_SHAPE;
+  if (mode == MK_GEMM_SWIGLU && N % mk::GN) return MK_ERR_BAD_SHAPE;
+  if (mode < 0 || mode > 3) return MK_ERR_BAD_ARG;
+  return MK_OK;
+}
+
+mk_status launch_attn(const DeviceState*, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
+                      int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
+  const int G = n_q / n_kv;
+  const int BQ = 16 * (8 / G);
+  AttnArgs a;
+  a.S = S;
+  a.n_q = n_q;
+  a.n_kv = n_kv;
+  a.ld_qkv = ld_qkv;
+  a.q_col = q_col;
+  a.k_col = k_col;
+  a.v_col = v_col;
+  a.ld_out = ld_out;
+  a.scale_log2 = scale_log2;
+  a.nqb = S / BQ;
+  dim3 grid(a.nqb, n_kv, bs);
+  const auto* q = static_cast<const __nv_bfloat16*>(qkv);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (hd == 96)
+    mk::attn_prefill_kernel<96><<<grid, mk::ATT_THREADS, mk::AttnShape<96>::SMEM, st>>>(q, o, a);
+  else
+    mk::attn_prefill_kernel<128><<<grid, mk::ATT_THREADS, mk::AttnShape<128>::SMEM, st>>>(q, o, a);
+  return cuda_status(cudaGetLastError());
+}
+
+mk_status check_attn_shape(int bs, int S, int n_q, int n_kv, int hd, int ld_qkv, int q_col, int k_col, int v_col,
+                           int ld_out) {
+  if (bs <= 0 || S <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv) return MK_ERR_BAD_SHAPE;
+  const int G = n_q / n_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return MK_ERR_BAD_SHAPE;
+  if (hd != 96 && hd != 128) return MK_ERR_BAD_SHAPE;
+  if (S % 128) return MK_ERR_BAD_SHAPE;
+  if (ld_qkv % 8 || q_col % 8 || k_col % 8 || v_col % 8 || ld_out % 8) return MK_ERR_BAD_ALIGN;
+  return MK_OK;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace
+
+struct mk_handle {
+  mk_config cfg;
+  int device = 0;
+  DeviceState* dev = nullptr;
+  bool bound = false;
+  mk_weight_ptrs w;
+  int n_qkv = 0, q_dim = 0, kv_dim = 0;
+  std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_down;  // per layer
+  CUtensorMap m_kv_last, m_q_last;
+};
+
+extern "C" {
+
+const char* mk_status_string(mk_status s) {
+  switch (s) {
+    case MK_OK: return "ok";
+    case MK_ERR_BAD_SHAPE: return "unsupported shape";
+    case MK_ERR_BAD_ALIGN: return "misaligned pointer or stride";
+    case MK_ERR_CUDA: return "CUDA error";
+    case MK_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case MK_ERR_BAD_ARG: return "bad argument";
+    case MK_ERR_NOT_BOUND: return "weights not bound";
+    case MK_ERR_BAD_TOKEN: return "token id out of range";
+    case MK_ERR_WORKSPACE: return "workspace too small";
+  }
+  return "unknown status";
+}
+
+int32_t mk_version(void) { return 100; }
+
+mk_status mk_create(const mk_config* cfg, int32_t device, mk_handle** out) {
+  if (!cfg || !out) return MK_ERR_BAD_ARG;
+  const mk_config& c = *cfg;
+  if (c.num_layers < 1 || c.hidden <= 0 || c.inter <= 0 || c.n_q <= 0 || c.n_kv <= 0 || c.vocab <= 0 ||
+      c.max_seq <= 0)
+    return MK_ERR_BAD_SHAPE;
+  if (c.head_dim != 96 && c.head_dim != 128) return MK_ERR_BAD_SHAPE;
+  if (c.n_q % c.n_kv) return MK_ERR_BAD_SHAPE;
+  const int G = c.n_q / c.n_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return MK_ERR_BAD_SHAPE;
+  const int n_qkv = (c.n_q + 2 * c.n_kv) * c.head_dim;
+  if (c.hidden % 128 || c.inter % 128 || (c.n_q * c.head_dim) % 128 || n_qkv % 128 ||
+      (2 * c.n_kv * c.head_dim) % 128)
+    return MK_ERR_BAD_SHAPE;
+  if (c.max_seq > 16384) return MK_ERR_BAD_SHAPE;
+  MK_CUDA(cudaSetDevice(device));
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  mk_handle* h = new mk_handle();
+  h->cfg = c;
+  h->device = device;
+  h->dev = d;
+  h->n_qkv = n_qkv;
+  h->q_dim = c.n_q * c.head_dim;
+  h->kv_dim = c.n_kv * c.head_dim;
+  *out = h;
+  return MK_OK;
+}
+
+mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
+  if (!h || !w) return MK_ERR_BAD_ARG;
+  const void* ptrs[] = {w->embed, w->lm_head, w->final_norm, w->rope_cos, w->rope_sin, w->w_qkv, w->s_qkv,
+                        w->w_o,   w->s_o,     w->w_gu,       w->s_gu,     w->w_down,   w->s_down};
+  for (const void* p : ptrs) {
+    if (!p) return MK_ERR_BAD_ARG;
+    if (!aligned16(p)) return MK_ERR_BAD_ALIGN;
+  }
+  MK_CUDA(cudaSetDevice(h->device));
+  const mk_config& c = h->cfg;
+  const int L = c.num_layers, H = c.hidden, I = c.inter;
+  h->m_qkv.resize(L);
+  h->m_o.resize(L);
+  h->m_gu.resize(L);
+  h->m_down.resize(L);
+  for (int l = 0; l < L; ++l) {
+    MK_TRY(map_b(&h->m_qkv[l], w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H, h->n_qkv, H));
+    MK_TRY(map_b(&h->m_o[l], w->w_o + static_cast<size_t>(l) * H * h->q_dim, H, h->q_dim));
+    MK_TRY(map_b(&h->m_gu[l], w->w_gu + static_cast<size_t>(l) * 2 * I * H, 2 * I, H));
+    MK_TRY(map_b(&h->m_down[l], w->w_down + static_cast<size_t>(l) * H * I, H, I));
+  }
+  const int8_t* wl = w->w_qkv + static_cast<size_t>(L - 1) * h->n_qkv * H;
+  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H));
+  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H, 2 * h->kv_dim, H));
+  h->w = *w;
+  h->bound = true;
+  return MK_OK;
+}
+
+namespace {
+struct Workspace {
+  size_t x, qkv, attn, hbuf, rstd, xl, ql, al, hl, rstdl, hf, logits, pval, pidx, top1, total;
+};
+
+Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
+  const mk_config& c = h->cfg;
+  const size_t T = static_cast<size_t>(bs) * seq;
+  Workspace w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  w.x = take(T * c.hidden * 2);
+  w.qkv = take(T * h->n_qkv * 2);
+  w.attn = take(T * h->q_dim * 2);
+  w.hbuf = take(T * c.inter * 2);
+  w.rstd = take(T * 4);
+  w.xl = take(static_cast<size_t>(bs) * c.hidden * 2);
+  w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
+  w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
+  w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
+  w.rstdl = take(static_cast<size_t>(bs) * 4);
+  w.hf = take(static_cast<size_t>(bs) * c.hidden * 4);
+  w.logits = take(static_cast<size_t>(bs) * c.vocab * 4);
+  w.pval = take(static_cast<size_t>(bs) * kLmParts * 4);
+  w.pidx = take(static_cast<size_t>(bs) * kLmParts * 4);
+  w.top1 = take(static_cast<size_t>(bs) * 4);
+  w.total = off;
+  return w;
+}
+
+mk_status lm_head_launch(const DeviceState*, const float* hf, int bs, int H, const void* lm, int V, float* logits,
+                         float* pval, int* pidx, int32_t* top1, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(mk::LM_ROWS) * H * 4;
+  if (smem > 96 * 1024) return MK_ERR_BAD_SHAPE;
+  for (int r0 = 0; r0 < bs; r0 += mk::LM_ROWS) {
+    mk::lm_head_kernel<<<kLmParts, mk::LM_THREADS, smem, st>>>(hf, static_cast<const __nv_bfloat16*>(lm), logits,
+                                                               pval, pidx, bs, H, V, r0);
+    MK_CUDA(cudaGetLastError());
+  }
+  mk::argmax_reduce_kernel<<<bs, 32, 0, st>>>(pval, pidx, kLmParts, top1);
+  return cuda_status(cudaGetLastError());
+}
+}  // namespace
+
+mk_status mk_workspace_size(const mk_handle* h, int32_t bs, int32_t seq, size_t* bytes) {
+  if (!h || !bytes) return MK_ERR_BAD_ARG;
+  if (bs <= 0 || seq <= 0) return MK_ERR_BAD_SHAPE;
+  *bytes = plan_workspace(h, bs, seq).total;
+  return MK_OK;
+}
+
+mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                     size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream) {
+  if (!h || !d_ids || !d_workspace) return MK_ERR_BAD_ARG;
+  if (!h->bound) return MK_ERR_NOT_BOUND;
+  const mk_config& c = h->cfg;
+  if (bs <= 0 || seq <= 0 || seq % 128 || seq > c.max_seq) return MK_ERR_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(d_workspace) & 255u) || !aligned16(d_ids)) return MK_ERR_BAD_ALIGN;
+  if ((d_hidden && !aligned16(d_hidden)) || (d_logits && !aligned16(d_logits))) return MK_ERR_BAD_ALIGN;
+  const Workspace ws = plan_workspace(h, bs, seq);
+  if (workspace_bytes < ws.total) return MK_ERR_WORKSPACE;
+  MK_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DeviceState* d = h->dev;
+  uint8_t* base = static_cast<uint8_t*>(d_workspace);
+  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(base + off); };
+  auto f32 = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
+
+  const int L = c.num_layers, H = c.hidden, I = c.inter, hd = c.head_dim;
+  const int T = bs * seq;
+  const int nqkv = h->n_qkv, qd = h->q_dim, kvd = h->kv_dim;
+  __nv_bfloat16 *x = bf(ws.x), *qkv = bf(ws.qkv), *attn = bf(ws.attn), *hb = bf(ws.hbuf);
+  __nv_bfloat16 *xl = bf(ws.xl), *ql = bf(ws.ql), *al = bf(ws.al), *hl = bf(ws.hl);
+  float *rstd = f32(ws.rstd), *rstdl = f32(ws.rstdl), *hf = f32(ws.hf);
+  float* logits = d_logits ? d_logits : f32(ws.logits);
+  int32_t* top1 = d_top1 ? d_top1 : reinterpret_cast<int32_t*>(base + ws.top1);
+  const float r = c.residual_scale;
+
+  CUtensorMap mx, mattn, mh, mxl, mal, mhl;
+  MK_TRY(map_a(&mx, x, T, H, H));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd));
+  MK_TRY(map_a(&mh, hb, T, I, I));
+  MK_TRY(map_a(&mxl, xl, bs, H, H));
+  MK_TRY(map_a(&mal, al, bs, qd, qd));
+  MK_TRY(map_a(&mhl, hl, bs, I, I));
+
+  const int rows_per_blk = 8;  // warps per 256-thread block, one row each
+  mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
+      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x, T, H, c.vocab, c.scale_emb, d->err);
+  MK_CUDA(cudaGetLastError());
+
+  auto rms = [&](const __nv_bfloat16* src, int rows, float* dst) -> mk_status {
+    mk::rms_rstd_kernel<<<(rows + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(src, dst, rows, H, H, c.eps);
+    return cuda_status(cudaGetLastError());
+  };
+  auto rope = [&](__nv_bfloat16* buf, int rows, int ld, int col0, int nh, int sq, int pos_base) -> mk_status {
+    const size_t work = static_cast<size_t>(rows) * nh * (hd / 4);
+    const int blocks = static_cast<int>(std::min<size_t>((work + 255) / 256, static_cast<size_t>(d->sm_count) * 16));
+    mk::rope_kernel<<<std::max(blocks, 1), 256, 0, st>>>(buf, h->w.rope_cos, h->w.rope_sin, rows, ld, col0, nh, hd,
+                                                        sq, pos_base);
+    return cuda_status(cudaGetLastError());
+  };
+
+  for (int l = 0; l < L - 1; ++l) {
+    MK_TRY(rms(x, T, rstd));
+    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, rstd,
+                       h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st));
+    MK_TRY(rope(qkv, T, nqkv, 0, c.n_q + c.n_kv, seq, 0));
+    MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
+    MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, MK_GEMM_RESID, nullptr, h->w.s_o + static_cast<size_t>(l) * H,
+                       x, H, r, st));
+    MK_TRY(rms(x, T, rstd));
+    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, rstd,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st));
+    MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, MK_GEMM_RESID, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, x, H, r, st));
+  }
+
+  // Last layer: K/V for every position, everything else for the last position only
+  // (`last_layer_step`, plugin/minicpm5_mk/mk_jax.py:492-520).
+  {
+    const int l = L - 1;
+    const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
+    __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
+    MK_TRY(rms(x, T, rstd));
+    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, rstd, sq + qd, kv, 2 * kvd, 0.f, st));
+    MK_TRY(rope(kv, T, 2 * kvd, 0, c.n_kv, seq, 0));
+    mk::gather_last_kernel<<<bs, 128, 0, st>>>(x, xl, bs, seq, H);
+    MK_CUDA(cudaGetLastError());
+    MK_TRY(rms(xl, bs, rstdl));
+    MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, rstdl, sq, ql, qd, 0.f, st));
+    MK_TRY(rope(ql, bs, qd, 0, c.n_q, 1, seq - 1));
+    AttnLastArgs la;
+    la.S = seq;
+    la.n_q = c.n_q;
+    la.n_kv = c.n_kv;
+    la.head_dim = hd;
+    la.ld_q = qd;
+    la.ld_kv = 2 * kvd;
+    la.k_col = 0;
+    la.v_col = kvd;
+    la.ld_out = qd;
+    la.scale_log2 = kLog2e;
+    const size_t smem = static_cast<size_t>(seq) * 4;
+    if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
+    mk::attn_last_kernel<<<dim3(c.n_q, bs), 256, smem, st>>>(ql, kv, al, la);
+    MK_CUDA(cudaGetLastError());
+    MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, MK_GEMM_RESID, nullptr, h->w.s_o + static_cast<size_t>(l) * H,
+                       xl, H, r, st));
+    MK_TRY(rms(xl, bs, rstdl));
+    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, rstdl,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st));
+    MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, MK_GEMM_RESID, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, xl, H, r, st));
+  }
+
+  mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
+                                            c.eps, c.logit_scale);
+  MK_CUDA(cudaGetLastError());
+  return lm_head_launch(d, hf, bs, H, h->w.lm_head, c.vocab, logits, f32(ws.pval),
+                        reinterpret_cast<int*>(base + ws.pidx), top1, st);
+}
+
+int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq) {
+  if (!h || bs <= 0 || seq <= 0) return 0;
+  const int per_layer = 8;   // rms, qkv gemm, rope, attention, o gemm, rms, gate/up gemm, down gemm
+  const int last_layer = 12; // rms, kv gemm, rope, gather, rms, q gemm, rope, attention, o, rms, gate/up, down
+  return 1 + (h->cfg.num_layers - 1) * per_layer + last_layer + 1 + (bs + mk::LM_ROWS - 1) / mk::LM_ROWS + 1;
+}
+
+mk_status mk_get_error(mk_handle* h, int32_t* device_err) {
+  if (h) MK_CUDA(cudaSetDevice(h->device));
+  MK_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  MK_CUDA(cudaMemcpyFromSymbol(&v, g_mk_err, sizeof(int)));
+  const int zero = 0;
+  MK_CUDA(cudaMemcpyToSymbol(g_mk_err, &zero, sizeof(int)));
+  if (device_err) *device_err = v;
+  if (v == 0) return MK_OK;
+  if (v == mk::DEV_ERR_BAD_TOKEN_ID) return MK_ERR_BAD_TOKEN;
+  return MK_ERR_DEVICE_TIMEOUT;
+}
+
+void mk_destroy(mk_handle* h) { delete h; }
+
+// ------------------------------------------------------------------------------ isolated kernels
+mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
+                        int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
+                        void* stream) {
+  if (!a || !w || !col_scale || !out) return MK_ERR_BAD_ARG;
+  MK_TRY(check_gemm_shape(M, N, K, mode));
+  if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  CUtensorMap ma, mb;
+  MK_TRY(map_a(&ma, a, M, K, lda));
+  MK_TRY(map_b(&mb, w, N, K));
+  return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
+                     static_cast<cudaStream_t>(stream));
+}
+
+mk_status mk_attention_prefill(const void* qkv, int32_t bs, int32_t seq, int32_t n_q, int32_t n_kv,
+                               int32_t head_dim, int32_t ld_qkv, int32_t q_col, int32_t k_col, int32_t v_col,
+                               float softmax_scale, void* out, int32_t ld_out, void* stream) {
+  if (!qkv || !out) return MK_ERR_BAD_ARG;
+  MK_TRY(check_attn_shape(bs, seq, n_q, n_kv, head_dim, ld_qkv, q_col, k_col, v_col, ld_out));
+  if (!aligned16(qkv) || !aligned16(out)) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  return launch_attn(d, qkv, bs, seq, n_q, n_kv, head_dim, ld_qkv, q_col, k_col, v_col, softmax_scale * kLog2e, out,
+                     ld_out, static_cast<cudaStream_t>(stream));
+}
+
+mk_status mk_rope(void* x, int32_t rows, int32_t ld, int32_t col0, int32_t n_heads, int32_t head_dim,
+                  const float* rope_cos, const float* rope_sin, int32_t seq, int32_t pos_base, void* stream) {
+  if (!x || !rope_cos || !rope_sin) return MK_ERR_BAD_ARG;
+  if (rows <= 0 || n_heads <= 0 || seq <= 0 || head_dim % 4 || pos_base < 0) return MK_ERR_BAD_SHAPE;
+  if (ld % 2 || col0 % 2 || (reinterpret_cast<uintptr_t>(x) & 3u)) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  const size_t work = static_cast<size_t>(rows) * n_heads * (head_dim / 4);
+  const int blocks = static_cast<int>(std::min<size_t>((work + 255) / 256, static_cast<size_t>(d->sm_count) * 16));
+  mk::rope_kernel<<<std::max(blocks, 1), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), rope_cos, rope_sin, rows, ld, col0, n_heads, head_dim, seq, pos_base);
+  return cuda_status(cudaGetLastError());
+}
+
+mk_status mk_rms_rstd(const void* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream) {
+  if (!x || !rstd) return MK_ERR_BAD_ARG;
+  if (T <= 0 || H <= 0 || H % 8) return MK_ERR_BAD_SHAPE;
+  if (!aligned16(x) || ld % 8) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  mk::rms_rstd_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), rstd, T, H, ld, eps);
+  return cuda_status(cudaGetLastError());
+}
+
+mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, void* x,
+                   void* stream) {
+  if (!ids || !embed || !x) return MK_ERR_BAD_ARG;
+  if (T <= 0 || V <= 0 || H <= 0 || H % 8) return MK_ERR_BAD_SHAPE;
+  if (!aligned16(embed) || !aligned16(x)) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  mk::embed_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16*>(embed), static_cast<__nv_bfloat16*>(x), T, H, V, scale, d->err);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t mk_lm_head_parts(void) { return kLmParts; }
+
+mk_status mk_lm_head_argmax(const float* hvec, int32_t bs, int32_t H, const void* lm_head, int32_t V, float* logits,
+                            float* part_val, int32_t* part_idx, int32_t* top1, void* stream) {
+  if (!hvec || !lm_head || !logits || !part_val || !part_idx || !top1) return MK_ERR_BAD_ARG;
+  if (bs <= 0 || H <= 0 || H % 8 || V <= 0) return MK_ERR_BAD_SHAPE;
+  if (!aligned16(lm_head)) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  return lm_head_launch(d, hvec, bs, H, lm_head, V, logits, part_val, part_idx, top1,
+                        static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

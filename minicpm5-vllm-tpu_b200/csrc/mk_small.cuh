@@ -1,0 +1,239 @@
+// HBM-bound kernels around the GEMMs: embedding gather, RMSNorm row statistics, RoPE,
+// last-row gather, final norm, lm_head + argmax.
+#pragma once
+
+#include "mk_common.cuh"
+
+namespace mk {
+
+// x[t, :] = bf16(scale * E[ids[t], :])        (`jnp.take(embed, ids)`, plugin/minicpm5_mk/mk_jax.py:532,
+// with the MiniCPM scale_emb).  One warp per token row, 16-byte vectors.  An id outside [0, V)
+// writes a zero row and records DEV_ERR_BAD_TOKEN_ID.
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
+                             __nv_bfloat16* __restrict__ x, int T, int H, int V, float scale, int* err) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int id = ids[row];
+  uint4* dst = reinterpret_cast<uint4*>(x + static_cast<size_t>(row) * H);
+  if (id < 0 || id >= V) {
+    if (lane == 0 && err) atomicCAS(err, 0, DEV_ERR_BAD_TOKEN_ID);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(E + static_cast<size_t>(id) * H);
+  for (int c = lane; c < H / 8; c += 32) {
+    uint4 v = __ldg(src + c);
+    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      w[e] = pack_bf16x2(f.x * scale, f.y * scale);
+    }
+    dst[c] = v;
+  }
+}
+
+// rstd[t] = rsqrt(mean(x[t]^2) + eps), f32 math (`rms_norm_unit`, plugin/minicpm5_mk/mk_jax.py:32-36).
+__global__ void rms_rstd_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ rstd, int T, int H,
+                                int ld, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ld);
+  float acc = 0.f;
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 v = __ldg(src + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      acc += f.x * f.x + f.y * f.y;
+    }
+  }
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  if (lane == 0) rstd[row] = rsqrtf(acc / static_cast<float>(H) + eps);
+}
+
+// In-place rotate_half RoPE on `n_heads` consecutive heads starting at column col0 of each row:
+//   x1' = x1 cos - x2 sin,  x2' = x2 cos + x1 sin      (benchmark/f32_golden.py:57-59, 88-89)
+// position of row r = pos_base + r % seq; cos/sin tables are f32 [max_seq, hd/2].
+// One thread per (row, head, pair of rotation indices).
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ x, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, int rows, int ld, int col0, int n_heads, int hd,
+                            int seq, int pos_base) {
+  const int half = hd / 2;
+  const int pairs = half / 2;  // two rotation indices per thread
+  const size_t total = static_cast<size_t>(rows) * n_heads * pairs;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(idx % pairs);
+    const size_t rh = idx / pairs;
+    const int h = static_cast<int>(rh % n_heads);
+    const int r = static_cast<int>(rh / n_heads);
+    const int pos = pos_base + r % seq;
+    const int i = 2 * p;
+    __nv_bfloat16* xp = x + static_cast<size_t>(r) * ld + col0 + h * hd;
+    const float2 c = *reinterpret_cast<const float2*>(cos_t + static_cast<size_t>(pos) * half + i);
+    const float2 s = *reinterpret_cast<const float2*>(sin_t + static_cast<size_t>(pos) * half + i);
+    const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xp + i));
+    const float2 b = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xp + half + i));
+    *reinterpret_cast<uint32_t*>(xp + i) = pack_bf16x2(a.x * c.x - b.x * s.x, a.y * c.y - b.y * s.y);
+    *reinterpret_cast<uint32_t*>(xp + half + i) = pack_bf16x2(b.x * c.x + a.x * s.x, b.y * c.y + a.y * s.y);
+  }
+}
+
+// xl[b, :] = x[b*S + S-1, :]  (the rows the last layer's token-local work needs).
+__global__ void gather_last_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xl, int bs,
+                                   int S, int H) {
+  const int b = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (static_cast<size_t>(b) * S + S - 1) * H);
+  uint4* dst = reinterpret_cast<uint4*>(xl + static_cast<size_t>(b) * H);
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+// hf[b, :] = logit_scale * x[b] * rsqrt(mean(x[b]^2) + eps) * w   (f32; final norm of
+// plugin/minicpm5_mk/mk_jax.py:569 with the logit scaling folded in); hidden[b, :] = bf16 of the
+// unscaled normed row when requested (the reference op's (bs, H) bf16 output).
+__global__ void final_norm_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                                  float* __restrict__ hf, __nv_bfloat16* __restrict__ hidden, int H, float eps,
+                                  float logit_scale) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(b) * H;
+  float acc = 0.f;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const float v = __bfloat162float(xr[k]);
+    acc += v * v;
+  }
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rs = rsqrtf(red[0] / static_cast<float>(H) + eps);
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const float v = __bfloat162float(xr[k]) * rs * w[k];
+    hf[static_cast<size_t>(b) * H + k] = v * logit_scale;
+    if (hidden) hidden[static_cast<size_t>(b) * H + k] = __float2bfloat16(v);
+  }
+}
+
+// logits[b, v] = sum_k hf[b, k] * W[v, k] (f32 accumulate, bf16 W [V, H]); per-CTA argmax
+// partials (value, lowest index on ties).  Rows are processed in groups of LM_ROWS so the f32
+// hidden rows fit in shared memory; each warp owns one vocab row at a time.
+constexpr int LM_ROWS = 8;
+constexpr int LM_THREADS = 256;
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(LM_THREADS)
+    lm_head_kernel(const float* __restrict__ hf, const __nv_bfloat16* __restrict__ W, float* __restrict__ logits,
+                   float* __restrict__ part_val, int* __restrict__ part_idx, int bs, int H, int V, int row0) {
+  extern __shared__ float lm_smem[];  // [LM_ROWS][H]
+  __shared__ float bval[LM_THREADS / 32][LM_ROWS];
+  __shared__ int bidx[LM_THREADS / 32][LM_ROWS];
+  const int nr = min(LM_ROWS, bs - row0);
+  for (int i = threadIdx.x; i < nr * H; i += blockDim.x) lm_smem[i] = hf[static_cast<size_t>(row0) * H + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float best[LM_ROWS];
+  int bi[LM_ROWS];
+#pragma unroll
+  for (int r = 0; r < LM_ROWS; ++r) {
+    best[r] = -INFINITY;
+    bi[r] = 0x7fffffff;
+  }
+  const int nwarps = gridDim.x * (LM_THREADS / 32);
+  for (int v = blockIdx.x * (LM_THREADS / 32) + warp; v < V; v += nwarps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + static_cast<size_t>(v) * H);
+    float acc[LM_ROWS];
+#pragma unroll
+    for (int r = 0; r < LM_ROWS; ++r) acc[r] = 0.f;
+    for (int c = lane; c < H / 8; c += 32) {
+      const uint4 wv = __ldg(wr + c);
+      const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+      float wf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w4[e]);
+        wf[2 * e] = f.x;
+        wf[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int r = 0; r < LM_ROWS; ++r) {
+        if (r < nr) {
+          const float* hr = lm_smem + r * H + c * 8;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r] += wf[e] * hr[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < LM_ROWS; ++r) {
+      float t = acc[r];
+      for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
+      if (r < nr) {
+        if (lane == 0) logits[static_cast<size_t>(row0 + r) * V + v] = t;
+        if (better(t, v, best[r], bi[r])) {
+          best[r] = t;
+          bi[r] = v;
+        }
+      }
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < LM_ROWS; ++r) {
+      bval[warp][r] = best[r];
+      bidx[warp][r] = bi[r];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nr) {
+    const int r = threadIdx.x;
+    float bv = bval[0][r];
+    int bb = bidx[0][r];
+    for (int w = 1; w < LM_THREADS / 32; ++w)
+      if (better(bval[w][r], bidx[w][r], bv, bb)) {
+        bv = bval[w][r];
+        bb = bidx[w][r];
+      }
+    part_val[static_cast<size_t>(row0 + r) * gridDim.x + blockIdx.x] = bv;
+    part_idx[static_cast<size_t>(row0 + r) * gridDim.x + blockIdx.x] = bb;
+  }
+}
+
+// top1[b] = argmax over the per-CTA partials of row b (warp-shuffle reduction, ties -> lowest id).
+__global__ void argmax_reduce_kernel(const float* __restrict__ part_val, const int* __restrict__ part_idx,
+                                     int nparts, int32_t* __restrict__ top1) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lane; i < nparts; i += 32) {
+    const float v = part_val[static_cast<size_t>(b) * nparts + i];
+    const int ix = part_idx[static_cast<size_t>(b) * nparts + i];
+    if (better(v, ix, bv, bi)) {
+      bv = v;
+      bi = ix;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffff, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) top1[b] = bi;
+}
+
+}  // namespace mk

@@ -59,8 +59,8 @@ class MkConfig:
             raise ValueError(f"head_dim {self.head_dim} not in (96, 128)")
         if self.n_q % self.n_kv:
             raise ValueError("n_q must be a multiple of n_kv")
-        if self.hidden % 128 or self.inter % 64 or self.q_dim % 128 or self.qkv_dim % 128:
-            raise ValueError("hidden % 128, inter % 64, n_q*head_dim % 128 and qkv width % 128 must be 0")
+        if self.hidden % 128 or self.inter % 128 or self.q_dim % 128 or self.qkv_dim % 128:
+            raise ValueError("hidden % 128, inter % 128, n_q*head_dim % 128 and qkv width % 128 must be 0")
         if (2 * self.n_kv * self.head_dim) % 128:
             raise ValueError("2*n_kv*head_dim must be a multiple of 128")
 

@@ -49,21 +49,27 @@ def param_shapes(cfg: MkConfig) -> Dict[str, Tuple[int, ...]]:
     return shapes
 
 
-def make_param(name: str, shape: Tuple[int, ...], seed: int = 1234, std: float = 0.02) -> torch.Tensor:
+def make_param(name: str, shape: Tuple[int, ...], seed: int = 1234, std: float = 0.02,
+               device: str | torch.device = "cpu") -> torch.Tensor:
+    """One tensor.  The CPU generator (default) is what the oracle and the parity tests use; a CUDA
+    device draws from that device's generator (same seeds, different values) to set up benchmark
+    replicas quickly."""
     if name.endswith("norm.weight"):
-        return torch.ones(shape, dtype=torch.float32)
-    g = torch.Generator().manual_seed(param_seed(seed, name))
-    return torch.randn(shape, generator=g, dtype=torch.float32) * std
+        return torch.ones(shape, dtype=torch.float32, device=device)
+    g = torch.Generator(device=device).manual_seed(param_seed(seed, name))
+    return torch.randn(shape, generator=g, dtype=torch.float32, device=device) * std
 
 
-def iter_random_weights(cfg: MkConfig, seed: int = 1234, std: float = 0.02) -> Iterator[Tuple[str, torch.Tensor]]:
-    """(name, fp32 CPU tensor) pairs in the order a checkpoint loader would yield them."""
+def iter_random_weights(cfg: MkConfig, seed: int = 1234, std: float = 0.02,
+                        device: str | torch.device = "cpu") -> Iterator[Tuple[str, torch.Tensor]]:
+    """(name, fp32 tensor) pairs in the order a checkpoint loader would yield them."""
     for name, shape in param_shapes(cfg).items():
-        yield name, make_param(name, shape, seed, std)
+        yield name, make_param(name, shape, seed, std, device)
 
 
-def random_state_dict(cfg: MkConfig, seed: int = 1234, std: float = 0.02) -> Dict[str, torch.Tensor]:
-    return dict(iter_random_weights(cfg, seed, std))
+def random_state_dict(cfg: MkConfig, seed: int = 1234, std: float = 0.02,
+                      device: str | torch.device = "cpu") -> Dict[str, torch.Tensor]:
+    return dict(iter_random_weights(cfg, seed, std, device))
 
 
 def synthetic_ids(bs: int, seq: int, seed: int = 1234, lo: int = 1000, hi: int = 30000,

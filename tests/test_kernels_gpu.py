@@ -1,0 +1,199 @@
+"""Per-kernel parity on a B200: each CUDA entry point of the C ABI against a plain PyTorch fp32
+reference of the same op on the same (seeded) inputs."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from minicpm5_mk import _lib
+    _lib.lib()
+    return torch.device("cuda", 0)
+
+
+def _gen(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+def _rand(shape, seed, scale=1.0):
+    return torch.randn(shape, generator=_gen(seed)) * scale
+
+
+def _quant(w):
+    from minicpm5_mk.mk_weights import quantize_per_out_channel
+    return quantize_per_out_channel(w)
+
+
+def _check_err():
+    from minicpm5_mk import _lib
+    import ctypes
+    e = ctypes.c_int32()
+    st = _lib.lib().mk_get_error(None, ctypes.byref(e))
+    assert st == 0 and e.value == 0, (st, hex(e.value))
+
+
+GEMM_CASES = [
+    # M, K, N
+    (128, 64, 256),
+    (256, 128, 384),
+    (300, 192, 256),
+    (2048, 1536, 1920),
+    (8192, 1536, 1536),
+    (1000, 4096, 1536),
+    (5, 1536, 1536),
+]
+
+
+@pytest.mark.parametrize("M,K,N", GEMM_CASES)
+@pytest.mark.parametrize("mode", ["colscale", "rowscale", "resid"])
+def test_gemm_w8a16(dev, M, K, N, mode):
+    from minicpm5_mk import ops, _lib
+    a = _rand((M, K), 1 + M + K).to(torch.bfloat16)
+    w8, s = _quant(_rand((N, K), 2 + N, 0.02))
+    rstd = torch.rand((M,), generator=_gen(3)) + 0.5
+    acc = a.float() @ w8.float().T
+    ad, wd, sd, rd = a.to(dev), w8.to(dev), s.to(dev), rstd.to(dev)
+    if mode == "colscale":
+        out = ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_COLSCALE)
+        ref = acc * s
+    elif mode == "rowscale":
+        out = ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_ROWSCALE, row_scale=rd)
+        ref = acc * rstd[:, None] * s
+    else:
+        x0 = _rand((M, N), 9).to(torch.bfloat16)
+        out = x0.to(dev).clone()
+        ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_RESID, resid_scale=0.3, out=out)
+        ref = x0.float() + 0.3 * acc * s
+    torch.cuda.synchronize()
+    _check_err()
+    got = out.float().cpu()
+    tol = 1e-2 * ref.abs().max().item() + 1e-3
+    err = (got - ref).abs().max().item()
+    assert err <= tol, (err, tol)
+    # bf16 output: almost every element within 1 bf16 ulp of the f32 reference
+    rel = ((got - ref).abs() / (ref.abs() + 1e-3)).flatten()
+    assert (rel > 1.6e-2).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("M,K,I", [(256, 128, 128), (777, 384, 512), (4096, 1536, 4608)])
+def test_gemm_swiglu(dev, M, K, I):
+    from minicpm5_mk import ops, _lib
+    from minicpm5_mk.mk_weights import interleave_gu
+    a = _rand((M, K), 11).to(torch.bfloat16)
+    g8, sg = _quant(_rand((I, K), 12, 0.05))
+    u8, su = _quant(_rand((I, K), 13, 0.05))
+    w8, s = interleave_gu(g8, u8), interleave_gu(sg, su)
+    rstd = torch.rand((M,), generator=_gen(14)) + 0.5
+    g = (a.float() @ g8.float().T) * rstd[:, None] * sg
+    u = (a.float() @ u8.float().T) * rstd[:, None] * su
+    ref = torch.nn.functional.silu(g) * u
+    out = ops.gemm_w8a16(a.to(dev), w8.to(dev), s.to(dev), _lib.MK_GEMM_SWIGLU, row_scale=rstd.to(dev))
+    torch.cuda.synchronize()
+    _check_err()
+    got = out.float().cpu()
+    assert got.shape == (M, I)
+    err = (got - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+def _attn_ref(qkv, bs, S, nq, nkv, hd, scale):
+    q = qkv[:, :nq * hd].float().reshape(bs, S, nq, hd).permute(0, 2, 1, 3)
+    k = qkv[:, nq * hd:(nq + nkv) * hd].float().reshape(bs, S, nkv, hd).permute(0, 2, 1, 3)
+    v = qkv[:, (nq + nkv) * hd:].float().reshape(bs, S, nkv, hd).permute(0, 2, 1, 3)
+    G = nq // nkv
+    k = k.repeat_interleave(G, dim=1)
+    v = v.repeat_interleave(G, dim=1)
+    s = torch.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    mask = torch.ones(S, S, dtype=torch.bool).tril()
+    s = s.masked_fill(~mask, float("-inf"))
+    o = torch.einsum("bhqk,bhkd->bhqd", torch.softmax(s, -1), v)
+    return o.permute(0, 2, 1, 3).reshape(bs * S, nq * hd)
+
+
+@pytest.mark.parametrize("bs,S,nq,nkv,hd", [
+    (1, 128, 16, 2, 96), (2, 512, 16, 2, 96), (1, 384, 4, 1, 128), (2, 256, 4, 2, 96), (1, 256, 8, 8, 128),
+    (1, 1024, 16, 2, 128),
+])
+def test_attention_prefill(dev, bs, S, nq, nkv, hd):
+    from minicpm5_mk import ops
+    qkv = _rand((bs * S, (nq + 2 * nkv) * hd), 21 + S + hd).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(hd)
+    out = ops.attention_prefill(qkv.to(dev), bs, S, nq, nkv, hd, softmax_scale=scale)
+    torch.cuda.synchronize()
+    _check_err()
+    ref = _attn_ref(qkv, bs, S, nq, nkv, hd, scale)
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2.5e-2, err
+
+
+def test_rope(dev):
+    from minicpm5_mk import ops
+    from minicpm5_mk.mk_weights import rope_tables
+    rows, nh, hd, S = 512, 6, 96, 256
+    cos, sin = rope_tables(1024, hd, 10000.0)
+    x = _rand((rows, nh * hd + 64), 31).to(torch.bfloat16)
+    y = x.to(dev).clone()
+    ops.rope_(y, nh, hd, cos.to(dev), sin.to(dev), S, col0=32)
+    torch.cuda.synchronize()
+    pos = torch.arange(rows) % S
+    xf = x.float()[:, 32:32 + nh * hd].reshape(rows, nh, hd)
+    h = hd // 2
+    c, s_ = cos[pos][:, None, :], sin[pos][:, None, :]
+    ref = torch.cat([xf[..., :h] * c - xf[..., h:] * s_, xf[..., h:] * c + xf[..., :h] * s_], -1).reshape(rows, -1)
+    got = y.float().cpu()
+    assert torch.equal(got[:, :32], x.float()[:, :32]) and torch.equal(got[:, 32 + nh * hd:], x.float()[:, 32 + nh * hd:])
+    assert (got[:, 32:32 + nh * hd] - ref).abs().max().item() <= 2e-2
+
+
+def test_rms_and_embed(dev):
+    from minicpm5_mk import ops
+    V, H, T = 1000, 384, 700
+    E = _rand((V, H), 41, 0.02).to(torch.bfloat16)
+    ids = torch.randint(0, V, (T,), generator=_gen(42), dtype=torch.int32)
+    x = ops.embed(ids.to(dev), E.to(dev), 12.0)
+    torch.cuda.synchronize()
+    ref = (E.float()[ids.long()] * 12.0).to(torch.bfloat16)
+    assert torch.equal(x.cpu(), ref)
+    r = ops.rms_rstd(x, 1e-6)
+    refr = torch.rsqrt(ref.float().pow(2).mean(-1) + 1e-6)
+    assert torch.allclose(r.cpu(), refr, rtol=1e-5, atol=0)
+    _check_err()
+
+
+def test_embed_bad_id_is_reported(dev):
+    from minicpm5_mk import ops, _lib
+    import ctypes
+    E = torch.ones((10, 64), dtype=torch.bfloat16, device=dev)
+    ids = torch.tensor([1, 10, 3], dtype=torch.int32, device=dev)
+    x = ops.embed(ids, E, 1.0)
+    e = ctypes.c_int32()
+    st = _lib.lib().mk_get_error(None, ctypes.byref(e))
+    assert st == 7 and e.value == 0x300
+    assert x[1].abs().sum().item() == 0 and x[0].float().sum().item() == 64
+    _check_err()  # cleared
+
+
+@pytest.mark.parametrize("bs,H,V", [(1, 1536, 73448), (3, 384, 1000), (11, 512, 2048)])
+def test_lm_head_argmax(dev, bs, H, V):
+    from minicpm5_mk import ops
+    h = _rand((bs, H), 51)
+    W = _rand((V, H), 52, 0.02).to(torch.bfloat16)
+    if V > 100:
+        W[V - 7] = W[17]  # planted exact tie: lowest id must win
+        h[0] = h[0].abs()
+        W[17] = W[17].abs() + 0.05
+        W[V - 7] = W[17]
+    logits, top1 = ops.lm_head_argmax(h.to(dev), W.to(dev))
+    torch.cuda.synchronize()
+    ref = h @ W.float().T
+    lg = logits.cpu()
+    assert (lg - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+    # argmax indexing is exact w.r.t. the kernel's own logits (ties -> lowest id)
+    assert torch.equal(top1.cpu().long(), torch.argmax(lg, dim=-1))
+    if V > 100:
+        assert int(top1[0]) == 17

@@ -48,10 +48,10 @@ def test_quantizer_matches_reference(golden_dir):
 
 
 def test_gu_interleave_roundtrip():
-    g = torch.arange(256 * 3).reshape(256, 3)
+    g = torch.arange(512 * 3).reshape(512, 3)
     u = -g
     x = mk_weights.interleave_gu(g, u)
-    assert torch.equal(x[:64], g[:64]) and torch.equal(x[64:128], u[:64])
+    assert torch.equal(x[:128], g[:128]) and torch.equal(x[128:256], u[:128])
     g2, u2 = mk_weights.deinterleave_gu(x)
     assert torch.equal(g2, g) and torch.equal(u2, u)
 
@@ -63,3 +63,21 @@ def test_rope_table_matches_golden_formula():
     half = cfg.head_dim // 2
     assert torch.equal(c, gc[:, :half]) and torch.equal(c, gc[:, half:])
     assert torch.equal(s, gs[:, :half])
+
+
+@pytest.mark.parametrize("preset,S", [("tiny-hd96", 256), ("tiny-hd128", 384)])
+def test_mirror_tracks_golden(preset, S):
+    """The int8 weight-only / bf16-activation design stays within the accuracy bar of the FP32 golden."""
+    from oracle import mirror
+    cfg = PRESETS[preset]
+    sd = random_state_dict(cfg, seed=1234)
+    pw = mk_weights.prepare_mk_weights(sd, cfg)
+    W = golden.golden_weights(sd, cfg)
+    ids = synthetic_ids(2, S, seed=3, vocab=cfg.vocab)
+    lg_m, _ = mirror.mirror_forward(ids, pw, cfg)
+    for b in range(2):
+        lg_g = golden.forward_logits(ids[b], W, cfg)
+        cos = torch.nn.functional.cosine_similarity(lg_g, lg_m[b], dim=0).item()
+        rng = (lg_g.max() - lg_g.min()).item()
+        assert cos >= 0.999, cos
+        assert (lg_g - lg_m[b]).abs().max().item() <= 2e-2 * rng
