@@ -49,7 +49,50 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_down", "attn"],
+                    help="time one isolated kernel of the forward (profiling driver) instead of the bench")
+    ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
+    ap.add_argument("--kernel-iters", type=int, default=3)
     return ap.parse_args()
+
+
+def run_kernel(a):
+    """Isolated launches of one forward kernel at the bench shapes (1 warm-up + --kernel-iters timed),
+    on random inputs; used as the small-case driver for ncu captures."""
+    from minicpm5_mk import _lib, ops
+    from minicpm5_mk.mk_config import get_config
+    from minicpm5_mk.mk_weights import quantize_per_out_channel
+
+    cfg = get_config(a.config)
+    dev = torch.device("cuda", 0)
+    T = a.kernel_bs * a.seq
+    g = torch.Generator(device=dev).manual_seed(3)
+    H, I = cfg.hidden, cfg.inter
+    if a.kernel.startswith("gemm"):
+        N, K, mode = {"gemm_swiglu": (2 * I, H, _lib.MK_GEMM_SWIGLU), "gemm_qkv": (cfg.qkv_dim, H, _lib.MK_GEMM_ROWSCALE),
+                      "gemm_down": (H, I, _lib.MK_GEMM_RESID)}[a.kernel]
+        x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
+        w8, s = quantize_per_out_channel(torch.randn((N, K), generator=g, device=dev) * 0.02)
+        rstd = torch.ones((T,), device=dev)
+        out = torch.zeros((T, N // 2 if mode == _lib.MK_GEMM_SWIGLU else N), dtype=torch.bfloat16, device=dev)
+        fn = lambda: ops.gemm_w8a16(x, w8, s, mode, row_scale=rstd, resid_scale=0.3, out=out)  # noqa: E731
+        flops = 2.0 * T * N * K
+    else:
+        qkv = torch.randn((T, cfg.qkv_dim), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((T, cfg.q_dim), dtype=torch.bfloat16, device=dev)
+        fn = lambda: ops.attention_prefill(qkv, a.kernel_bs, a.seq, cfg.n_q, cfg.n_kv, cfg.head_dim,  # noqa: E731
+                                           softmax_scale=cfg.head_dim ** -0.5, out=out)
+        flops = 2.0 * a.seq * a.seq * cfg.head_dim * cfg.n_q * a.kernel_bs
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.kernel_iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.kernel_iters
+    print(json.dumps({"kernel": a.kernel, "tokens": T, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1)}))
 
 
 def _peaks():
@@ -186,6 +229,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
         run_reference(a, rank, world)
+        return
+    if a.kernel:
+        run_kernel(a)
         return
     import torch.distributed as dist
     from datetime import timedelta
