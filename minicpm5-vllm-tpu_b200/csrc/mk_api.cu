@@ -11,6 +11,7 @@
 
 #include "../../include/minicpm5_mk.h"
 #include "mk_attn.cuh"
+#include "mk_attn_tc.cuh"
 #include "mk_common.cuh"
 #include "mk_gemm.cuh"
 #include "mk_small.cuh"
@@ -72,6 +73,10 @@ mk_status device_state(DeviceState** out) {
                                  static_cast<int>(mk::AttnShape<96>::SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::AttnShape<128>::SMEM)));
+    MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::TA_SMEM)));
+    MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::TA_SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_last_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
     MK_CUDA(cudaFuncSetAttribute(mk::lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
     if (!g_encode) {
@@ -141,8 +146,56 @@ mk_status check_gemm_shape(int M, int N, int K, int mode) {
   return MK_OK;
 }
 
-mk_status launch_attn(const DeviceState*, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
+// bf16 [T, ld] viewed as [T, heads, hd] (3D), box 64 x box_heads x box_rows, 128-byte swizzle.
+mk_status map_heads(CUtensorMap* m, const void* base, int T, int heads, int hd, int ld, int box_heads,
+                    int box_rows) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_heads), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
+}
+
+int ilog2(int v) {
+  int r = 0;
+  while ((1 << r) < v) ++r;
+  return r;
+}
+
+// tcgen05 causal GQA attention (mk_attn_tc.cuh).
+mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
                       int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
+  const int G = n_q / n_kv;
+  const int qpt = 128 / G;
+  if (S % (2 * qpt) || S % mk::TA_BK) return MK_ERR_BAD_SHAPE;
+  const int T = bs * S;
+  const auto* base = static_cast<const __nv_bfloat16*>(qkv);
+  CUtensorMap mq, mkm, mv;
+  MK_TRY(map_heads(&mq, base + q_col, T, n_q, hd, ld_qkv, G, qpt));
+  MK_TRY(map_heads(&mkm, base + k_col, T, n_kv, hd, ld_qkv, 1, mk::TA_BK));
+  MK_TRY(map_heads(&mv, base + v_col, T, n_kv, hd, ld_qkv, 1, mk::TA_BK));
+  mk::AttnTcArgs a;
+  a.S = S;
+  a.lg2G = ilog2(G);
+  a.nqb = S / (2 * qpt);
+  a.ld_out = ld_out;
+  a.scale_log2 = scale_log2;
+  a.err = d->err;
+  dim3 grid(a.nqb, n_kv, bs);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (hd == 96)
+    mk::attn_tc_kernel<96><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
+  else
+    mk::attn_tc_kernel<128><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
+  return cuda_status(cudaGetLastError());
+}
+
+// mma.sync attention (mk_attn.cuh), kept as the reference point of the first version.
+mk_status launch_attn_mma(const DeviceState*, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
+                          int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
   const int G = n_q / n_kv;
   const int BQ = 16 * (8 / G);
   AttnArgs a;
@@ -174,6 +227,7 @@ mk_status check_attn_shape(int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
   if (hd != 96 && hd != 128) return MK_ERR_BAD_SHAPE;
   if (S % 128) return MK_ERR_BAD_SHAPE;
   if (ld_qkv % 8 || q_col % 8 || k_col % 8 || v_col % 8 || ld_out % 8) return MK_ERR_BAD_ALIGN;
+  if (S % (256 / G)) return MK_ERR_BAD_SHAPE;  // two 128-row (query x head) tiles per CTA
   return MK_OK;
 }
 

@@ -117,7 +117,7 @@ def _attn_ref(qkv, bs, S, nq, nkv, hd, scale):
 
 @pytest.mark.parametrize("bs,S,nq,nkv,hd", [
     (1, 128, 16, 2, 96), (2, 512, 16, 2, 96), (1, 384, 4, 1, 128), (2, 256, 4, 2, 96), (1, 256, 8, 8, 128),
-    (1, 1024, 16, 2, 128),
+    (1, 1024, 16, 2, 128), (3, 640, 16, 2, 96),
 ])
 def test_attention_prefill(dev, bs, S, nq, nkv, hd):
     from minicpm5_mk import ops
@@ -129,6 +129,32 @@ def test_attention_prefill(dev, bs, S, nq, nkv, hd):
     ref = _attn_ref(qkv, bs, S, nq, nkv, hd, scale)
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 2.5e-2, err
+
+
+@pytest.mark.parametrize("hd", [96, 128])
+def test_attention_prefill_full_length(dev, hd):
+    """BASELINE isolated-attention shape (seq 8192, 16 Q / 2 KV heads) against a plain PyTorch fp32
+    reference evaluated on the GPU in 1024-query chunks."""
+    from minicpm5_mk import ops
+    S, nq, nkv = 8192, 16, 2
+    g = torch.Generator(device=dev).manual_seed(77 + hd)
+    qkv = torch.randn((S, (nq + 2 * nkv) * hd), generator=g, device=dev).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(hd)
+    out = ops.attention_prefill(qkv, 1, S, nq, nkv, hd, softmax_scale=scale)
+    torch.cuda.synchronize()
+    _check_err()
+    q = qkv[:, :nq * hd].float().reshape(S, nq, hd)
+    k = qkv[:, nq * hd:(nq + nkv) * hd].float().reshape(S, nkv, hd).repeat_interleave(nq // nkv, dim=1)
+    v = qkv[:, (nq + nkv) * hd:].float().reshape(S, nkv, hd).repeat_interleave(nq // nkv, dim=1)
+    worst = 0.0
+    for q0 in range(0, S, 1024):
+        q1 = q0 + 1024
+        s = torch.einsum("qhd,khd->hqk", q[q0:q1], k[:q1]) * scale
+        mask = torch.arange(q1, device=dev)[None, :] <= torch.arange(q0, q1, device=dev)[:, None]
+        s = s.masked_fill(~mask[None], float("-inf"))
+        o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v[:q1]).reshape(1024, nq * hd)
+        worst = max(worst, (out[q0:q1].float() - o).abs().max().item())
+    assert worst < 2.5e-2, worst
 
 
 def test_rope(dev):
