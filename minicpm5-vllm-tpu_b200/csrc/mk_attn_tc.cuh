@@ -11,29 +11,34 @@
 //
 //   warp 0      TMA producer: Q0/Q1 once (3D map over [token, head, dim], 128B swizzle), then a
 //               2-stage ring of K and V tiles (K: K-major operand; V: MN-major operand)
-//   warp 1      TMEM allocator + single-thread MMA issuer, per key tile j:
-//                 S_t = Q_t K_j^T  (t = 0, 1)       M=128, N=128, K=head_dim   -> TMEM cols [128t, 128t+128)
-//                 O_t += P_t V_j                      M=128, N=head_dim, K=128 (P_t read from TMEM)
+//   warp 1      TMEM allocator + single-thread MMA issuer.  For 64-key tile j it issues
+//                 S_t(j+1) = Q_t K_{j+1}^T into the other S buffer of tile t  (M=128, N=64, K=hd)
+//                 O_t += P_t(j) V_j  once the softmax has written P_t(j)        (M=128, N=hd, K=64)
+//               so the tensor core computes the next scores while the softmax works on this tile.
 //   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: thread i owns row i of S_t
-//               (TMEM lane i).  Pass 1 takes the row max, pass 2 writes P = exp2(S*c - m) as bf16
-//               pairs over the S columns it has already read (P_t aliases S_t).  The running max
-//               is only moved (and O_t rescaled in TMEM) when it grows by more than 2^8, so
-//               rescaling is rare; P stays <= 256.  At the end the same threads normalise O_t by the
-//               row sum and store bf16 rows.
+//               (TMEM lane i), loads its 64 scores once, takes the max, writes P = exp2(S*c - m) as
+//               bf16 pairs over the same TMEM columns (P_t aliases S_t).  The running max is only
+//               moved (and O_t rescaled in TMEM) when it grows by more than 2^8, so rescaling is
+//               rare; P stays <= 256.  At the end the same threads normalise O_t by the row sum and
+//               store bf16 rows.
 //
-// TMEM: S0 [0,128) S1 [128,256) O0 [256, 256+hd) O1 [384, 384+hd) of a 512-column allocation.
-// Shared memory: Q 2 tiles x 2 chunks, K and V 2 stages x 2 chunks, each chunk 128 rows x 128 B.
-// head_dim 96 uses a second 64-column chunk whose upper 32 columns are TMA zero-fill / unread.
+// TMEM (512 columns): S_t[b] at [128t + 64b, +64) for tile t and buffer b; O_t at [256 + 128t, +hd).
+// Shared memory: Q 2 tiles x 2 chunks (128 rows x 128 B each), K and V 4 stages x 2 chunks
+// (64 rows x 128 B each).  head_dim 96 uses a second 64-column chunk whose upper 32 columns are
+// TMA zero-fill and never read by the MMAs.
 #pragma once
 
 #include "mk_common.cuh"
 
 namespace mk {
 
-constexpr int TA_BK = 128;
+constexpr int TA_BK = 64;
+constexpr int TA_STAGES = 4;
 constexpr int TA_THREADS = 384;
-constexpr uint32_t TA_CHUNK = 128 * 128;  // 128 rows x 128 bytes
-constexpr size_t TA_SMEM = 1024 + 12 * TA_CHUNK + 256;
+constexpr uint32_t TA_QCHUNK = 128 * 128;   // 128 rows x 128 bytes
+constexpr uint32_t TA_KCHUNK = TA_BK * 128;  // 64 rows x 128 bytes
+constexpr uint32_t TA_STAGE = 4 * TA_KCHUNK;  // K (2 chunks) + V (2 chunks)
+constexpr size_t TA_SMEM = 1024 + 4 * TA_QCHUNK + TA_STAGES * TA_STAGE + 256;
 constexpr float TA_RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 struct AttnTcArgs {
@@ -53,19 +58,18 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   extern __shared__ uint8_t ta_smem_raw[];
   const uint32_t raw = smem_u32(ta_smem_raw);
   uint8_t* sbase = ta_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sQ = sbase;                  // [tile][chunk]
-  uint8_t* sK = sbase + 4 * TA_CHUNK;   // [stage][chunk]
-  uint8_t* sV = sbase + 8 * TA_CHUNK;   // [stage][chunk]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + 12 * TA_CHUNK);
+  uint8_t* sQ = sbase;                    // [tile][chunk], 16 KB each
+  uint8_t* sKV = sbase + 4 * TA_QCHUNK;   // [stage]{K chunk 0, K chunk 1, V chunk 0, V chunk 1}, 8 KB each
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + TA_STAGES * TA_STAGE);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;     // [2]
-  uint64_t* v_full = bars + 3;     // [2]
-  uint64_t* kv_empty = bars + 5;   // [2]
-  uint64_t* s_full = bars + 7;     // [2] per Q tile
-  uint64_t* p_ready = bars + 9;    // [2]
-  uint64_t* pv_done = bars + 11;   // [2]
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;                  // [TA_STAGES]
+  uint64_t* v_full = k_full + TA_STAGES;        // [TA_STAGES]
+  uint64_t* kv_empty = v_full + TA_STAGES;      // [TA_STAGES]
+  uint64_t* s_full = kv_empty + TA_STAGES;      // [2 tiles][2 buffers]
+  uint64_t* p_ready = s_full + 4;               // [2 tiles][2 buffers]
+  uint64_t* pv_done = p_ready + 4;              // [2 tiles]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -79,14 +83,17 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < TA_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 4);
-      mbar_init(&pv_done[i], 1);
     }
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -107,31 +114,29 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     if (lane == 0) {
       // ---------------------------------------------------------------- TMA producer
       uint32_t issued = 0, issued_par = 0;  // bit s: stage s has loads in flight / their parity
-      bool q_issued = false;
-      mbar_arrive_expect_tx(q_full, 4 * TA_CHUNK);
+      mbar_arrive_expect_tx(q_full, 4 * TA_QCHUNK);
       for (int t = 0; t < 2; ++t)
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(sQ + (t * 2 + c) * TA_CHUNK, &tmQ, q_full, c * 64, g * G, tok0 + q0 + t * qpt);
-      q_issued = true;
+          tma_load_3d(sQ + (t * 2 + c) * TA_QCHUNK, &tmQ, q_full, c * 64, g * G, tok0 + q0 + t * qpt);
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[s], 2 * TA_CHUNK);
+        const int st = j % TA_STAGES;
+        const uint32_t ph = (j / TA_STAGES) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag)) break;
+        uint8_t* sst = sKV + st * TA_STAGE;
+        mbar_arrive_expect_tx(&k_full[st], 2 * TA_KCHUNK);
+        for (int c = 0; c < 2; ++c) tma_load_3d(sst + c * TA_KCHUNK, &tmK, &k_full[st], c * 64, g, tok0 + j * TA_BK);
+        mbar_arrive_expect_tx(&v_full[st], 2 * TA_KCHUNK);
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(sK + (s * 2 + c) * TA_CHUNK, &tmK, &k_full[s], c * 64, g, tok0 + j * TA_BK);
-        mbar_arrive_expect_tx(&v_full[s], 2 * TA_CHUNK);
-        for (int c = 0; c < 2; ++c)
-          tma_load_3d(sV + (s * 2 + c) * TA_CHUNK, &tmV, &v_full[s], c * 64, g, tok0 + j * TA_BK);
-        issued |= 1u << s;
-        issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          tma_load_3d(sst + (2 + c) * TA_KCHUNK, &tmV, &v_full[st], c * 64, g, tok0 + j * TA_BK);
+        issued |= 1u << st;
+        issued_par = (issued_par & ~(1u << st)) | (ph << st);
       }
       // every issued copy must land before the CTA exits
-      if (q_issued) mbar_wait_drain(q_full, 0);
-      for (int s = 0; s < 2; ++s)
-        if (issued & (1u << s)) {
-          mbar_wait_drain(&k_full[s], (issued_par >> s) & 1u);
-          mbar_wait_drain(&v_full[s], (issued_par >> s) & 1u);
+      mbar_wait_drain(q_full, 0);
+      for (int st = 0; st < TA_STAGES; ++st)
+        if (issued & (1u << st)) {
+          mbar_wait_drain(&k_full[st], (issued_par >> st) & 1u);
+          mbar_wait_drain(&v_full[st], (issued_par >> st) & 1u);
         }
     }
   } else if (warp == 1) {
@@ -139,47 +144,58 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, TA_BK);
       constexpr uint32_t idesc_pv = idesc_bf16_f32_bmn(128, HD);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[s], ph, abort_flag)) break;
+      // S_t(j) = Q_t K_j^T into S buffer j & 1 of tile t
+      auto issue_s = [&](int j) {
+        const int st = j % TA_STAGES;
+        const uint8_t* kb = sKV + st * TA_STAGE;
         for (int t = 0; t < 2; ++t) {
-          // S_t / P_t of the previous tile must be consumed by O_t += P_t V before S_t is rewritten
-          if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + t * 128;
+          const uint32_t d = tmem + t * 128 + (j & 1) * 64;
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
             const int c = ks >> 2;
-            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_CHUNK)) + 2 * (ks & 3);
-            const uint64_t db = sdesc_kmajor_sw128(smem_u32(sK + (s * 2 + c) * TA_CHUNK)) + 2 * (ks & 3);
+            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_QCHUNK)) + 2 * (ks & 3);
+            const uint64_t db = sdesc_kmajor_sw128(smem_u32(kb + c * TA_KCHUNK)) + 2 * (ks & 3);
             mma_f16_ss(d, da, db, idesc_s, ks > 0 ? 1u : 0u);
           }
-          mma_commit(&s_full[t]);
+          mma_commit(&s_full[t * 2 + (j & 1)]);
         }
-        if (!ok || !mbar_wait(&v_full[s], ph, abort_flag)) break;
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j % TA_STAGES;
+        if (j + 1 < ntiles) {
+          const int j1 = j + 1;
+          if (!mbar_wait(&k_full[j1 % TA_STAGES], (j1 / TA_STAGES) & 1, abort_flag)) break;
+          // S buffer (j+1)&1 still holds P_t(j-1): O_t += P_t(j-1) V must have finished
+          if (j1 >= 2 && (!mbar_wait(&pv_done[0], (j - 1) & 1, abort_flag) ||
+                          !mbar_wait(&pv_done[1], (j - 1) & 1, abort_flag)))
+            break;
+          tc_fence_after();
+          issue_s(j1);
+        }
+        if (!mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag)) break;
+        const uint32_t vb = smem_u32(sKV + st * TA_STAGE + 2 * TA_KCHUNK);
         for (int t = 0; t < 2; ++t) {
-          if (!mbar_wait(&p_ready[t], j & 1, abort_flag)) {
+          if (!mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem + 256 + t * 128;
-          const uint32_t pa = tmem + t * 128;
-          const uint32_t vb = smem_u32(sV + s * 2 * TA_CHUNK);
+          const uint32_t pa = tmem + t * 128 + (j & 1) * 64;
 #pragma unroll
           for (int ks = 0; ks < TA_BK / 16; ++ks) {
-            const uint64_t db = sdesc_mnmajor_sw128(vb + ks * 2048, TA_CHUNK);
+            const uint64_t db = sdesc_mnmajor_sw128(vb + ks * 2048, TA_KCHUNK);
             mma_f16_ts(d, pa + ks * 8, db, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(&pv_done[t]);
         }
         if (!ok) break;
-        mma_commit(&kv_empty[s]);
+        mma_commit(&kv_empty[st]);
       }
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
@@ -198,27 +214,25 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[t * 2 + b], (j >> 1) & 1, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      uint32_t v[64];
+      tmem_ld_32x32b_x32(tS + b * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld_32x32b_x32(tS + b * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld_wait();
       const int valid = query - j * TA_BK + 1;  // keys of this tile visible to this row
+      if (valid < TA_BK) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e)
+          if (e >= valid) v[e] = __float_as_uint(-INFINITY);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < TA_BK / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
-        if (valid >= TA_BK) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
-      }
+      for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
       const float m_tile = mx * sc;
       const bool need = m_tile > m_used + TA_RESCALE_THRESHOLD;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -231,48 +245,30 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         const float alpha = need ? ex2_approx(m_used - m_tile) : 1.f;
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tO + c * 32, v);
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-          tmem_st_32x32b_x32(tO + c * 32, v);
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + c * 32, o);
         }
         tmem_st_wait();
         l *= alpha;
       }
       if (need) m_used = m_tile;
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < TA_BK / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
-        uint32_t pk[16];
-        if (valid >= TA_BK) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sc, -m_used));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sc, -m_used));
-            l += p0 + p1;
-            pk[e] = pack_bf16x2(p0, p1);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int k0 = c * 32 + 2 * e;
-            const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e]), sc, -m_used)) : 0.f;
-            const float p1 = k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sc, -m_used)) : 0.f;
-            l += p0 + p1;
-            pk[e] = pack_bf16x2(p0, p1);
-          }
-        }
-        // P columns [16c, 16c+16) overwrite S columns already read
-        tmem_st_32x32b_x16(tS + c * 16, pk);
+      for (int e = 0; e < 32; ++e) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sc, -m_used));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sc, -m_used));
+        l += p0 + p1;
+        pk[e] = pack_bf16x2(p0, p1);
       }
+      tmem_st_32x32b_x32(tS + b * 64, pk);  // P_t(j) over the S columns just read
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[t]);
+      if (lane == 0) mbar_arrive(&p_ready[t * 2 + b]);
     }
     if (ok && mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag)) {
       tc_fence_after();
@@ -280,13 +276,13 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + query) * a.ld_out + head * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tO + c * 32, v);
+        uint32_t o32[32];
+        tmem_ld_32x32b_x32(tO + c * 32, o32);
         tmem_ld_wait();
         uint32_t o[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-          o[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
+          o[e] = pack_bf16x2(__uint_as_float(o32[2 * e]) * inv, __uint_as_float(o32[2 * e + 1]) * inv);
         uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
         for (int q = 0; q < 4; ++q) d4[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
