@@ -124,16 +124,18 @@ typedef enum mk_gemm_mode {
   MK_GEMM_ROWSCALE = 0, /* out = bf16(acc * row_scale[m] * col_scale[n])                     */
   MK_GEMM_RESID = 1,    /* out = bf16(out + resid_scale * acc * col_scale[n])   (in place)   */
   MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g) * u) over 128-row gate/up blocks; out width N/2 */
-  MK_GEMM_COLSCALE = 3  /* out = bf16(acc * col_scale[n])                                    */
+  MK_GEMM_COLSCALE = 3, /* out = bf16(acc * col_scale[n])                                    */
+  MK_GEMM_RESID32 = 4   /* resid32 += resid_scale * acc * col_scale[n] (f32, in place); out = bf16(resid32) */
 } mk_gemm_mode;
 
 /* W8A16 GEMM: acc[m, n] = sum_k a[m, k] * w[n, k]; a bf16 [M, lda], w int8 [N, K].
  * N % 128 == 0 (N % 256 == 0 for SWIGLU), K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
+ * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream.
  * Replaces `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` (mk_jax.py:233-269) and the
  * gate/up half of `fused_mlp` (mk_mlp.py:68-145). */
 mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
                         int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
-                        void* stream);
+                        float* resid32, int32_t ld_resid32, void* stream);
 
 /* Causal GQA prefill attention over bs sequences of length seq.  qkv bf16 [bs*seq, ld_qkv] with
  * Q heads at column q_col, K at k_col, V at v_col (each head head_dim wide); out bf16
@@ -150,12 +152,13 @@ mk_status mk_attention_prefill(const void* qkv, int32_t bs, int32_t seq, int32_t
 mk_status mk_rope(void* x, int32_t rows, int32_t ld, int32_t col0, int32_t n_heads, int32_t head_dim,
                   const float* rope_cos, const float* rope_sin, int32_t seq, int32_t pos_base, void* stream);
 
-/* rstd[t] = 1/sqrt(mean(x[t, :H]^2) + eps)  (`rms_norm_unit`, plugin/minicpm5_mk/mk_jax.py:32-36). */
-mk_status mk_rms_rstd(const void* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream);
+/* rstd[t] = 1/sqrt(mean(x[t, :H]^2) + eps) for the f32 residual stream x [T, ld]
+ * (`rms_norm_unit`, plugin/minicpm5_mk/mk_jax.py:32-36). */
+mk_status mk_rms_rstd(const float* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream);
 
-/* x[t] = bf16(scale * embed[ids[t]])  (plugin/minicpm5_mk/mk_jax.py:532). */
-mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, void* x,
-                   void* stream);
+/* x32[t] = scale * embed[ids[t]] (f32) and xb[t] = bf16(x32[t])  (plugin/minicpm5_mk/mk_jax.py:532). */
+mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, float* x32,
+                   void* xb, void* stream);
 
 /* logits[b] = h[b] @ lm_head^T (f32), top1[b] = argmax (ties -> lowest id) for h f32 [bs, H].
  * part_val/part_idx: scratch of bs * mk_lm_head_parts() entries each.

@@ -120,7 +120,7 @@ mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K) {
 
 mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
                       int mode, const float* row_scale, const float* col_scale, void* out, int ldo, float resid,
-                      cudaStream_t st) {
+                      cudaStream_t st, float* resid32 = nullptr, int ld_resid32 = 0) {
   GemmArgs ga;
   ga.M = M;
   ga.N = N;
@@ -131,6 +131,8 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.out = static_cast<__nv_bfloat16*>(out);
   ga.ldo = ldo;
   ga.resid_scale = resid;
+  ga.resid32 = resid32;
+  ga.ld_resid32 = ld_resid32;
   ga.err = d->err;
   const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
@@ -142,7 +144,7 @@ mk_status check_gemm_shape(int M, int N, int K, int mode) {
   if (M <= 0 || N <= 0 || K <= 0) return MK_ERR_BAD_SHAPE;
   if (N % 128 || K % mk::GK) return MK_ERR_BAD_SHAPE;
   if (mode == MK_GEMM_SWIGLU && N % mk::GN) return MK_ERR_BAD_SHAPE;
-  if (mode < 0 || mode > 3) return MK_ERR_BAD_ARG;
+  if (mode < 0 || mode > 4) return MK_ERR_BAD_ARG;
   return MK_OK;
 }
 
@@ -327,7 +329,7 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
 
 namespace {
 struct Workspace {
-  size_t x, qkv, attn, hbuf, rstd, xl, ql, al, hl, rstdl, hf, logits, pval, pidx, top1, total;
+  size_t x32, xb, qkv, attn, hbuf, rstd, xl32, xlb, ql, al, hl, rstdl, hf, logits, pval, pidx, top1, total;
 };
 
 Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
@@ -340,12 +342,14 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
     off = align256(off + bytes);
     return o;
   };
-  w.x = take(T * c.hidden * 2);
+  w.x32 = take(T * c.hidden * 4);
+  w.xb = take(T * c.hidden * 2);
   w.qkv = take(T * h->n_qkv * 2);
   w.attn = take(T * h->q_dim * 2);
   w.hbuf = take(T * c.inter * 2);
   w.rstd = take(T * 4);
-  w.xl = take(static_cast<size_t>(bs) * c.hidden * 2);
+  w.xl32 = take(static_cast<size_t>(bs) * c.hidden * 4);
+  w.xlb = take(static_cast<size_t>(bs) * c.hidden * 2);
   w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
@@ -400,27 +404,29 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   const int L = c.num_layers, H = c.hidden, I = c.inter, hd = c.head_dim;
   const int T = bs * seq;
   const int nqkv = h->n_qkv, qd = h->q_dim, kvd = h->kv_dim;
-  __nv_bfloat16 *x = bf(ws.x), *qkv = bf(ws.qkv), *attn = bf(ws.attn), *hb = bf(ws.hbuf);
-  __nv_bfloat16 *xl = bf(ws.xl), *ql = bf(ws.ql), *al = bf(ws.al), *hl = bf(ws.hl);
+  // f32 residual stream (x32 / xl32) with bf16 copies (xb / xlb) feeding the projections
+  float *x32 = f32(ws.x32), *xl32 = f32(ws.xl32);
+  __nv_bfloat16 *xb = bf(ws.xb), *qkv = bf(ws.qkv), *attn = bf(ws.attn), *hb = bf(ws.hbuf);
+  __nv_bfloat16 *xlb = bf(ws.xlb), *ql = bf(ws.ql), *al = bf(ws.al), *hl = bf(ws.hl);
   float *rstd = f32(ws.rstd), *rstdl = f32(ws.rstdl), *hf = f32(ws.hf);
   float* logits = d_logits ? d_logits : f32(ws.logits);
   int32_t* top1 = d_top1 ? d_top1 : reinterpret_cast<int32_t*>(base + ws.top1);
   const float r = c.residual_scale;
 
   CUtensorMap mx, mattn, mh, mxl, mal, mhl;
-  MK_TRY(map_a(&mx, x, T, H, H));
+  MK_TRY(map_a(&mx, xb, T, H, H));
   MK_TRY(map_a(&mattn, attn, T, qd, qd));
   MK_TRY(map_a(&mh, hb, T, I, I));
-  MK_TRY(map_a(&mxl, xl, bs, H, H));
+  MK_TRY(map_a(&mxl, xlb, bs, H, H));
   MK_TRY(map_a(&mal, al, bs, qd, qd));
   MK_TRY(map_a(&mhl, hl, bs, I, I));
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
   mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
-      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x, T, H, c.vocab, c.scale_emb, d->err);
+      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err);
   MK_CUDA(cudaGetLastError());
 
-  auto rms = [&](const __nv_bfloat16* src, int rows, float* dst) -> mk_status {
+  auto rms = [&](const float* src, int rows, float* dst) -> mk_status {
     mk::rms_rstd_kernel<<<(rows + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(src, dst, rows, H, H, c.eps);
     return cuda_status(cudaGetLastError());
   };
@@ -433,18 +439,18 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   };
 
   for (int l = 0; l < L - 1; ++l) {
-    MK_TRY(rms(x, T, rstd));
+    MK_TRY(rms(x32, T, rstd));
     MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, rstd,
                        h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st));
     MK_TRY(rope(qkv, T, nqkv, 0, c.n_q + c.n_kv, seq, 0));
     MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
-    MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, MK_GEMM_RESID, nullptr, h->w.s_o + static_cast<size_t>(l) * H,
-                       x, H, r, st));
-    MK_TRY(rms(x, T, rstd));
+    MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
+                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
+    MK_TRY(rms(x32, T, rstd));
     MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, rstd,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st));
-    MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, MK_GEMM_RESID, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, x, H, r, st));
+    MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
   }
 
   // Last layer: K/V for every position, everything else for the last position only
@@ -453,12 +459,12 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     const int l = L - 1;
     const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
     __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
-    MK_TRY(rms(x, T, rstd));
+    MK_TRY(rms(x32, T, rstd));
     MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, rstd, sq + qd, kv, 2 * kvd, 0.f, st));
     MK_TRY(rope(kv, T, 2 * kvd, 0, c.n_kv, seq, 0));
-    mk::gather_last_kernel<<<bs, 128, 0, st>>>(x, xl, bs, seq, H);
+    mk::gather_last_kernel<<<bs, 256, 0, st>>>(x32, xl32, xlb, bs, seq, H);
     MK_CUDA(cudaGetLastError());
-    MK_TRY(rms(xl, bs, rstdl));
+    MK_TRY(rms(xl32, bs, rstdl));
     MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, rstdl, sq, ql, qd, 0.f, st));
     MK_TRY(rope(ql, bs, qd, 0, c.n_q, 1, seq - 1));
     AttnLastArgs la;
@@ -476,16 +482,16 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
     mk::attn_last_kernel<<<dim3(c.n_q, bs), 256, smem, st>>>(ql, kv, al, la);
     MK_CUDA(cudaGetLastError());
-    MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, MK_GEMM_RESID, nullptr, h->w.s_o + static_cast<size_t>(l) * H,
-                       xl, H, r, st));
-    MK_TRY(rms(xl, bs, rstdl));
+    MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
+                       h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
+    MK_TRY(rms(xl32, bs, rstdl));
     MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, rstdl,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st));
-    MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, MK_GEMM_RESID, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, xl, H, r, st));
+    MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
   }
 
-  mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
+  mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
                                             c.eps, c.logit_scale);
   MK_CUDA(cudaGetLastError());
   return lm_head_launch(d, hf, bs, H, h->w.lm_head, c.vocab, logits, f32(ws.pval),
@@ -517,10 +523,12 @@ void mk_destroy(mk_handle* h) { delete h; }
 // ------------------------------------------------------------------------------ isolated kernels
 mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
                         int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
-                        void* stream) {
+                        float* resid32, int32_t ld_resid32, void* stream) {
   if (!a || !w || !col_scale || !out) return MK_ERR_BAD_ARG;
   MK_TRY(check_gemm_shape(M, N, K, mode));
   if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
+  if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned16(resid32) || ld_resid32 % 4 || ld_resid32 < N))
+    return resid32 ? MK_ERR_BAD_ALIGN : MK_ERR_BAD_ARG;
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
@@ -528,7 +536,7 @@ mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const 
   MK_TRY(map_a(&ma, a, M, K, lda));
   MK_TRY(map_b(&mb, w, N, K));
   return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
-                     static_cast<cudaStream_t>(stream));
+                     static_cast<cudaStream_t>(stream), resid32, ld_resid32);
 }
 
 mk_status mk_attention_prefill(const void* qkv, int32_t bs, int32_t seq, int32_t n_q, int32_t n_kv,
@@ -557,26 +565,26 @@ mk_status mk_rope(void* x, int32_t rows, int32_t ld, int32_t col0, int32_t n_hea
   return cuda_status(cudaGetLastError());
 }
 
-mk_status mk_rms_rstd(const void* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream) {
+mk_status mk_rms_rstd(const float* x, int32_t T, int32_t H, int32_t ld, float eps, float* rstd, void* stream) {
   if (!x || !rstd) return MK_ERR_BAD_ARG;
   if (T <= 0 || H <= 0 || H % 8) return MK_ERR_BAD_SHAPE;
-  if (!aligned16(x) || ld % 8) return MK_ERR_BAD_ALIGN;
+  if (!aligned16(x) || ld % 4) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
   mk::rms_rstd_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), rstd, T, H, ld, eps);
+      x, rstd, T, H, ld, eps);
   return cuda_status(cudaGetLastError());
 }
 
-mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, void* x,
-                   void* stream) {
-  if (!ids || !embed || !x) return MK_ERR_BAD_ARG;
+mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, float* x32,
+                   void* xb, void* stream) {
+  if (!ids || !embed || !x32 || !xb) return MK_ERR_BAD_ARG;
   if (T <= 0 || V <= 0 || H <= 0 || H % 8) return MK_ERR_BAD_SHAPE;
-  if (!aligned16(embed) || !aligned16(x)) return MK_ERR_BAD_ALIGN;
+  if (!aligned16(embed) || !aligned16(x32) || !aligned16(xb)) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
   mk::embed_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, static_cast<const __nv_bfloat16*>(embed), static_cast<__nv_bfloat16*>(x), T, H, V, scale, d->err);
+      ids, static_cast<const __nv_bfloat16*>(embed), x32, static_cast<__nv_bfloat16*>(xb), T, H, V, scale, d->err);
   return cuda_status(cudaGetLastError());
 }
 

@@ -7,7 +7,10 @@
 // Epilogue modes (the per-row / per-column scalings commute with the sum, so they are applied to
 // the f32 accumulator read back from TMEM):
 //   ROWSCALE : out = bf16(acc * rstd[m] * s[n])                   RMSNorm-fused projections (QKV)
-//   RESID    : out = bf16(out + r * acc * s[n])   (in place)       o_proj / down + scaled residual
+//   RESID    : out = bf16(out + r * acc * s[n])   (in place)       bf16 residual
+//   RESID32  : x32 = x32 + r * acc * s[n] (f32, in place), out = bf16(x32)
+//              o_proj / down + scaled residual on the f32 residual stream; `out` is the bf16 copy
+//              the next projection reads as its A operand
 //   SWIGLU   : tile = 128 gate + 128 up channels (interleaved weight rows);
 //              h[m, i] = bf16(silu(g * rstd[m] * s_g) * (u * rstd[m] * s_u))   (out width N/2)
 //
@@ -28,7 +31,7 @@
 
 namespace mk {
 
-enum GemmMode : int { GEMM_ROWSCALE = 0, GEMM_RESID = 1, GEMM_SWIGLU = 2, GEMM_COLSCALE = 3 };
+enum GemmMode : int { GEMM_ROWSCALE = 0, GEMM_RESID = 1, GEMM_SWIGLU = 2, GEMM_COLSCALE = 3, GEMM_RESID32 = 4 };
 
 constexpr int GM = 128;   // rows of A per tile (UMMA M)
 constexpr int GN = 256;   // output channels per tile (UMMA N)
@@ -52,6 +55,8 @@ struct GemmArgs {
   __nv_bfloat16* out;      // [M, ldo]
   int ldo;
   float resid_scale;
+  float* resid32;          // [M, ld_resid32] (RESID32)
+  int ld_resid32;
   int* err;
 };
 
@@ -222,7 +227,21 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             const float* sc = args.col_scale + n0 + c0;
             uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
             uint32_t o[16];
-            if (args.mode == GEMM_RESID) {
+            if (args.mode == GEMM_RESID32) {
+              float4* xr = reinterpret_cast<float4*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0);
+              const float r = args.resid_scale;
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                float4 x = xr[v];
+                x.x += r * (__uint_as_float(acc[4 * v + 0]) * __ldg(sc + 4 * v + 0));
+                x.y += r * (__uint_as_float(acc[4 * v + 1]) * __ldg(sc + 4 * v + 1));
+                x.z += r * (__uint_as_float(acc[4 * v + 2]) * __ldg(sc + 4 * v + 2));
+                x.w += r * (__uint_as_float(acc[4 * v + 3]) * __ldg(sc + 4 * v + 3));
+                xr[v] = x;
+                o[2 * v] = pack_bf16x2(x.x, x.y);
+                o[2 * v + 1] = pack_bf16x2(x.z, x.w);
+              }
+            } else if (args.mode == GEMM_RESID) {
               uint4 xin[4];
 #pragma unroll
               for (int v = 0; v < 4; ++v) xin[v] = dst[v];

@@ -6,50 +6,58 @@
 
 namespace mk {
 
-// x[t, :] = bf16(scale * E[ids[t], :])        (`jnp.take(embed, ids)`, plugin/minicpm5_mk/mk_jax.py:532,
-// with the MiniCPM scale_emb).  One warp per token row, 16-byte vectors.  An id outside [0, V)
-// writes a zero row and records DEV_ERR_BAD_TOKEN_ID.
+// x32[t, :] = scale * E[ids[t], :] (f32 residual stream) and xb = bf16(x32) (the projections' A
+// operand) -- `jnp.take(embed, ids)`, plugin/minicpm5_mk/mk_jax.py:532, with the MiniCPM scale_emb.
+// One warp per token row, 16-byte vectors.  An id outside [0, V) writes a zero row and records
+// DEV_ERR_BAD_TOKEN_ID.
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
-                             __nv_bfloat16* __restrict__ x, int T, int H, int V, float scale, int* err) {
+                             float* __restrict__ x32, __nv_bfloat16* __restrict__ xb, int T, int H, int V, float scale,
+                             int* err) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const int id = ids[row];
-  uint4* dst = reinterpret_cast<uint4*>(x + static_cast<size_t>(row) * H);
+  uint4* db = reinterpret_cast<uint4*>(xb + static_cast<size_t>(row) * H);
+  float4* d32 = reinterpret_cast<float4*>(x32 + static_cast<size_t>(row) * H);
   if (id < 0 || id >= V) {
     if (lane == 0 && err) atomicCAS(err, 0, DEV_ERR_BAD_TOKEN_ID);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
+    for (int c = lane; c < H / 8; c += 32) {
+      db[c] = make_uint4(0, 0, 0, 0);
+      d32[2 * c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      d32[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     return;
   }
   const uint4* src = reinterpret_cast<const uint4*>(E + static_cast<size_t>(id) * H);
   for (int c = lane; c < H / 8; c += 32) {
     uint4 v = __ldg(src + c);
     uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+    float f[8];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16x2(w[e]);
-      w[e] = pack_bf16x2(f.x * scale, f.y * scale);
+      const float2 p = unpack_bf16x2(w[e]);
+      f[2 * e] = p.x * scale;
+      f[2 * e + 1] = p.y * scale;
+      w[e] = pack_bf16x2(f[2 * e], f[2 * e + 1]);
     }
-    dst[c] = v;
+    db[c] = v;
+    d32[2 * c] = make_float4(f[0], f[1], f[2], f[3]);
+    d32[2 * c + 1] = make_float4(f[4], f[5], f[6], f[7]);
   }
 }
 
-// rstd[t] = rsqrt(mean(x[t]^2) + eps), f32 math (`rms_norm_unit`, plugin/minicpm5_mk/mk_jax.py:32-36).
-__global__ void rms_rstd_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ rstd, int T, int H,
-                                int ld, float eps) {
+// rstd[t] = rsqrt(mean(x[t]^2) + eps) over the f32 residual stream (`rms_norm_unit`,
+// plugin/minicpm5_mk/mk_jax.py:32-36).  One warp per row.
+__global__ void rms_rstd_kernel(const float* __restrict__ x, float* __restrict__ rstd, int T, int H, int ld,
+                                float eps) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
-  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ld);
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * ld);
   float acc = 0.f;
-  for (int c = lane; c < H / 8; c += 32) {
-    const uint4 v = __ldg(src + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16x2(w[e]);
-      acc += f.x * f.x + f.y * f.y;
-    }
+  for (int c = lane; c < H / 4; c += 32) {
+    const float4 v = __ldg(src + c);
+    acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
   if (lane == 0) rstd[row] = rsqrtf(acc / static_cast<float>(H) + eps);
@@ -83,27 +91,29 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, const float* __restri
   }
 }
 
-// xl[b, :] = x[b*S + S-1, :]  (the rows the last layer's token-local work needs).
-__global__ void gather_last_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xl, int bs,
-                                   int S, int H) {
+// xl32[b, :] = x32[b*S + S-1, :], xlb = bf16 copy (the rows the last layer's token-local work needs).
+__global__ void gather_last_kernel(const float* __restrict__ x32, float* __restrict__ xl32,
+                                   __nv_bfloat16* __restrict__ xlb, int bs, int S, int H) {
   const int b = blockIdx.x;
-  const uint4* src = reinterpret_cast<const uint4*>(x + (static_cast<size_t>(b) * S + S - 1) * H);
-  uint4* dst = reinterpret_cast<uint4*>(xl + static_cast<size_t>(b) * H);
-  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+  const float* src = x32 + (static_cast<size_t>(b) * S + S - 1) * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    const float v = src[c];
+    xl32[static_cast<size_t>(b) * H + c] = v;
+    xlb[static_cast<size_t>(b) * H + c] = __float2bfloat16(v);
+  }
 }
 
 // hf[b, :] = logit_scale * x[b] * rsqrt(mean(x[b]^2) + eps) * w   (f32; final norm of
 // plugin/minicpm5_mk/mk_jax.py:569 with the logit scaling folded in); hidden[b, :] = bf16 of the
 // unscaled normed row when requested (the reference op's (bs, H) bf16 output).
-__global__ void final_norm_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
-                                  float* __restrict__ hf, __nv_bfloat16* __restrict__ hidden, int H, float eps,
-                                  float logit_scale) {
+__global__ void final_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ hf,
+                                  __nv_bfloat16* __restrict__ hidden, int H, float eps, float logit_scale) {
   __shared__ float red[32];
   const int b = blockIdx.x;
-  const __nv_bfloat16* xr = x + static_cast<size_t>(b) * H;
+  const float* xr = x + static_cast<size_t>(b) * H;
   float acc = 0.f;
   for (int k = threadIdx.x; k < H; k += blockDim.x) {
-    const float v = __bfloat162float(xr[k]);
+    const float v = xr[k];
     acc += v * v;
   }
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
@@ -117,7 +127,7 @@ __global__ void final_norm_kernel(const __nv_bfloat16* __restrict__ x, const flo
   __syncthreads();
   const float rs = rsqrtf(red[0] / static_cast<float>(H) + eps);
   for (int k = threadIdx.x; k < H; k += blockDim.x) {
-    const float v = __bfloat162float(xr[k]) * rs * w[k];
+    const float v = xr[k] * rs * w[k];
     hf[static_cast<size_t>(b) * H + k] = v * logit_scale;
     if (hidden) hidden[static_cast<size_t>(b) * H + k] = __float2bfloat16(v);
   }

@@ -18,7 +18,7 @@ EXPORTED = (
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward",
 )
 
-MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE = 0, 1, 2, 3
+MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
 
 _i32, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -61,12 +61,13 @@ def lib() -> ctypes.CDLL:
         L.mk_get_error.argtypes = [_vp, ctypes.POINTER(_i32)]
         L.mk_destroy.restype = None
         L.mk_destroy.argtypes = [_vp]
-        L.mk_gemm_w8a16.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _vp]
+        L.mk_gemm_w8a16.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _vp, _i32,
+                                    _vp]
         L.mk_attention_prefill.argtypes = [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp,
                                            _i32, _vp]
         L.mk_rope.argtypes = [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp]
         L.mk_rms_rstd.argtypes = [_vp, _i32, _i32, _i32, _f32, _vp, _vp]
-        L.mk_embed.argtypes = [_vp, _i32, _vp, _i32, _i32, _f32, _vp, _vp]
+        L.mk_embed.argtypes = [_vp, _i32, _vp, _i32, _i32, _f32, _vp, _vp, _vp]
         L.mk_lm_head_parts.restype = _i32
         L.mk_lm_head_parts.argtypes = []
         L.mk_lm_head_argmax.argtypes = [_vp, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp]

@@ -120,8 +120,9 @@ class MkEngine:
 # ----------------------------------------------------------------------------------- per-stage ops
 def gemm_w8a16(a: torch.Tensor, w: torch.Tensor, col_scale: torch.Tensor, mode: int,
                row_scale: Optional[torch.Tensor] = None, resid_scale: float = 1.0,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """acc = a @ w^T (a bf16 [M, K], w int8 [N, K]) with the epilogue `mode` (see _lib.MK_GEMM_*)."""
+               out: Optional[torch.Tensor] = None, resid32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """acc = a @ w^T (a bf16 [M, K], w int8 [N, K]) with the epilogue `mode` (see _lib.MK_GEMM_*).
+    RESID32 updates the f32 residual `resid32` in place and writes its bf16 copy to `out`."""
     for t, n in ((a, "a"), (w, "w"), (col_scale, "col_scale")):
         _cuda(t, n)
     M, K = a.shape
@@ -131,6 +132,7 @@ def gemm_w8a16(a: torch.Tensor, w: torch.Tensor, col_scale: torch.Tensor, mode: 
         out = torch.empty((M, width), dtype=torch.bfloat16, device=a.device)
     st = _lib.lib().mk_gemm_w8a16(a.data_ptr(), M, K, a.stride(0), w.data_ptr(), col_scale.data_ptr(), N, mode,
                                   _ptr(row_scale), float(resid_scale), out.data_ptr(), out.stride(0),
+                                  _ptr(resid32), resid32.stride(0) if resid32 is not None else 0,
                                   _stream(a.device))
     _lib.check(st, "mk_gemm_w8a16")
     return out
@@ -161,6 +163,9 @@ def rope_(x: torch.Tensor, n_heads: int, head_dim: int, cos: torch.Tensor, sin: 
 
 
 def rms_rstd(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """x: f32 [T, H] residual stream."""
+    if x.dtype != torch.float32:
+        raise ValueError("minicpm5_mk: rms_rstd expects the f32 residual stream")
     out = torch.empty((x.shape[0],), dtype=torch.float32, device=x.device)
     st = _lib.lib().mk_rms_rstd(x.data_ptr(), x.shape[0], x.shape[1], x.stride(0), float(eps), out.data_ptr(),
                                 _stream(x.device))
@@ -168,14 +173,16 @@ def rms_rstd(x: torch.Tensor, eps: float) -> torch.Tensor:
     return out
 
 
-def embed(ids: torch.Tensor, table: torch.Tensor, scale: float) -> torch.Tensor:
+def embed(ids: torch.Tensor, table: torch.Tensor, scale: float):
+    """Returns (x32 f32 [T, H], xb bf16 [T, H])."""
     _cuda(ids, "ids")
     _cuda(table, "embed")
-    out = torch.empty((ids.numel(), table.shape[1]), dtype=torch.bfloat16, device=ids.device)
+    x32 = torch.empty((ids.numel(), table.shape[1]), dtype=torch.float32, device=ids.device)
+    xb = torch.empty((ids.numel(), table.shape[1]), dtype=torch.bfloat16, device=ids.device)
     st = _lib.lib().mk_embed(ids.data_ptr(), ids.numel(), table.data_ptr(), table.shape[0], table.shape[1],
-                             float(scale), out.data_ptr(), _stream(ids.device))
+                             float(scale), x32.data_ptr(), xb.data_ptr(), _stream(ids.device))
     _lib.check(st, "mk_embed")
-    return out
+    return x32, xb
 
 
 def lm_head_argmax(h: torch.Tensor, w: torch.Tensor):

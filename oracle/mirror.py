@@ -1,9 +1,10 @@
 """CPU numerics mirror of the B200 path (TEST INFRASTRUCTURE ONLY -- see oracle/golden.py header).
 
 The same forward as oracle/golden.py, but on the prepared int8 weight-only weights and with bf16
-rounding at exactly the points where the CUDA kernels round (activations stored in bf16, f32
-accumulation, f32 scales applied in the GEMM epilogue, attention probabilities rounded to bf16
-before P @ V in the prefill kernel).  It lets the GPU parity tests use tolerances near bf16
+rounding at exactly the points where the CUDA kernels round: the residual stream stays f32 and its
+bf16 copy feeds the projections; projection outputs (q/k/v, attention output, SiLU(g)*u) are stored
+in bf16; f32 accumulation; f32 scales applied in the GEMM epilogue; attention probabilities rounded
+to bf16 before P @ V in the prefill kernel.  It lets the GPU parity tests use tolerances near bf16
 resolution, separately from the accuracy of the design against the FP32 golden.
 
 It follows the same reference steps as oracle/golden.py (benchmark/f32_golden.py:78-102) and the
@@ -82,38 +83,38 @@ def mirror_forward(ids: torch.Tensor, pw: dict, cfg):
     E = pw["embed"].to(F32)
     logits_all, hidden_all = [], []
     for b in range(bs):
-        x = bf(E[ids[b].long()] * cfg.scale_emb)
+        x = E[ids[b].long()] * cfg.scale_emb  # f32 residual stream
         for l in range(L - 1):
             Wqkv, sqkv = _deq(pw["w_qkv"][l]), pw["s_qkv"][l]
-            qkv = bf((x @ Wqkv.T) * _rstd(x, cfg.eps) * sqkv)
+            qkv = bf((bf(x) @ Wqkv.T) * _rstd(x, cfg.eps) * sqkv)
             q = _rope(qkv[:, :qd].reshape(S, nq, hd), cos, sin)
             k = _rope(qkv[:, qd:qd + kvd].reshape(S, nkv, hd), cos, sin)
             v = qkv[:, qd + kvd:].reshape(S, nkv, hd)
             a = _attn_prefill(q, k, v, G)
-            x = bf(x + r * ((a @ _deq(pw["w_o"][l]).T) * pw["s_o"][l]))
-            gu = (x @ _deq(pw["w_gu"][l]).T) * _rstd(x, cfg.eps) * pw["s_gu"][l]
+            x = x + r * ((a @ _deq(pw["w_o"][l]).T) * pw["s_o"][l])
+            gu = (bf(x) @ _deq(pw["w_gu"][l]).T) * _rstd(x, cfg.eps) * pw["s_gu"][l]
             g, u = _deinterleave(gu.T)
             h = bf(torch.nn.functional.silu(g.T) * u.T)
-            x = bf(x + r * ((h @ _deq(pw["w_down"][l]).T) * pw["s_down"][l]))
+            x = x + r * ((h @ _deq(pw["w_down"][l]).T) * pw["s_down"][l])
         l = L - 1
         Wqkv, sqkv = _deq(pw["w_qkv"][l]), pw["s_qkv"][l]
         rs = _rstd(x, cfg.eps)
-        kv = bf((x @ Wqkv[qd:].T) * rs * sqkv[qd:])
+        kv = bf((bf(x) @ Wqkv[qd:].T) * rs * sqkv[qd:])
         k = _rope(kv[:, :kvd].reshape(S, nkv, hd), cos, sin)
         v = kv[:, kvd:].reshape(S, nkv, hd)
         xl = x[-1:]
-        ql = bf((xl @ Wqkv[:qd].T) * _rstd(xl, cfg.eps) * sqkv[:qd])
+        ql = bf((bf(xl) @ Wqkv[:qd].T) * _rstd(xl, cfg.eps) * sqkv[:qd])
         ql = _rope(ql.reshape(1, nq, hd), cos[-1:], sin[-1:])[0]
         kr = k.repeat_interleave(G, dim=1)
         vr = v.repeat_interleave(G, dim=1)
         s = torch.einsum("hd,khd->hk", ql, kr)
         p = torch.softmax(s, dim=-1)
         al = bf(torch.einsum("hk,khd->hd", p, vr).reshape(1, qd))
-        xl = bf(xl + r * ((al @ _deq(pw["w_o"][l]).T) * pw["s_o"][l]))
-        gu = (xl @ _deq(pw["w_gu"][l]).T) * _rstd(xl, cfg.eps) * pw["s_gu"][l]
+        xl = xl + r * ((al @ _deq(pw["w_o"][l]).T) * pw["s_o"][l])
+        gu = (bf(xl) @ _deq(pw["w_gu"][l]).T) * _rstd(xl, cfg.eps) * pw["s_gu"][l]
         g, u = _deinterleave(gu.T)
         h = bf(torch.nn.functional.silu(g.T) * u.T)
-        xl = bf(xl + r * ((h @ _deq(pw["w_down"][l]).T) * pw["s_down"][l]))
+        xl = xl + r * ((h @ _deq(pw["w_down"][l]).T) * pw["s_down"][l])
         hn = xl * _rstd(xl, cfg.eps) * pw["final_norm"]
         logits_all.append((hn * cfg.logit_scale) @ pw["lm_head"].to(F32).T)
         hidden_all.append(hn)

@@ -50,7 +50,7 @@ GEMM_CASES = [
 
 
 @pytest.mark.parametrize("M,K,N", GEMM_CASES)
-@pytest.mark.parametrize("mode", ["colscale", "rowscale", "resid"])
+@pytest.mark.parametrize("mode", ["colscale", "rowscale", "resid", "resid32"])
 def test_gemm_w8a16(dev, M, K, N, mode):
     from minicpm5_mk import ops, _lib
     a = _rand((M, K), 1 + M + K).to(torch.bfloat16)
@@ -64,11 +64,20 @@ def test_gemm_w8a16(dev, M, K, N, mode):
     elif mode == "rowscale":
         out = ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_ROWSCALE, row_scale=rd)
         ref = acc * rstd[:, None] * s
-    else:
+    elif mode == "resid":
         x0 = _rand((M, N), 9).to(torch.bfloat16)
         out = x0.to(dev).clone()
         ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_RESID, resid_scale=0.3, out=out)
         ref = x0.float() + 0.3 * acc * s
+    else:
+        x0 = _rand((M, N), 9)
+        x32 = x0.to(dev).clone()
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_RESID32, resid_scale=0.3, out=out, resid32=x32)
+        ref = x0 + 0.3 * acc * s
+        torch.cuda.synchronize()
+        assert (x32.cpu() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item() + 1e-5
+        assert torch.equal(out.cpu(), x32.cpu().to(torch.bfloat16))
     torch.cuda.synchronize()
     _check_err()
     got = out.float().cpu()
@@ -181,12 +190,13 @@ def test_rms_and_embed(dev):
     V, H, T = 1000, 384, 700
     E = _rand((V, H), 41, 0.02).to(torch.bfloat16)
     ids = torch.randint(0, V, (T,), generator=_gen(42), dtype=torch.int32)
-    x = ops.embed(ids.to(dev), E.to(dev), 12.0)
+    x32, xb = ops.embed(ids.to(dev), E.to(dev), 12.0)
     torch.cuda.synchronize()
-    ref = (E.float()[ids.long()] * 12.0).to(torch.bfloat16)
-    assert torch.equal(x.cpu(), ref)
-    r = ops.rms_rstd(x, 1e-6)
-    refr = torch.rsqrt(ref.float().pow(2).mean(-1) + 1e-6)
+    ref32 = E.float()[ids.long()] * 12.0
+    assert torch.equal(x32.cpu(), ref32)
+    assert torch.equal(xb.cpu(), ref32.to(torch.bfloat16))
+    r = ops.rms_rstd(x32, 1e-6)
+    refr = torch.rsqrt(ref32.pow(2).mean(-1) + 1e-6)
     assert torch.allclose(r.cpu(), refr, rtol=1e-5, atol=0)
     _check_err()
 
@@ -196,11 +206,11 @@ def test_embed_bad_id_is_reported(dev):
     import ctypes
     E = torch.ones((10, 64), dtype=torch.bfloat16, device=dev)
     ids = torch.tensor([1, 10, 3], dtype=torch.int32, device=dev)
-    x = ops.embed(ids, E, 1.0)
+    x32, xb = ops.embed(ids, E, 1.0)
     e = ctypes.c_int32()
     st = _lib.lib().mk_get_error(None, ctypes.byref(e))
     assert st == 7 and e.value == 0x300
-    assert x[1].abs().sum().item() == 0 and x[0].float().sum().item() == 64
+    assert xb[1].abs().sum().item() == 0 and x32[1].abs().sum().item() == 0 and x32[0].sum().item() == 64
     _check_err()  # cleared
 
 

@@ -44,5 +44,5 @@ def test_bad_arguments_are_status_codes():
     assert L.mk_forward(None, None, 1, 128, None, 0, None, None, None, None) == 5
     assert L.mk_launches_per_forward(None, 1, 128) == 0
     # shape checks run before any device work
-    assert L.mk_gemm_w8a16(8, 128, 100, 128, 8, 8, 256, 0, 8, 1.0, 8, 256, None) == 1  # K % 64
+    assert L.mk_gemm_w8a16(8, 128, 100, 128, 8, 8, 256, 0, 8, 1.0, 8, 256, None, 0, None) == 1  # K % 64
     assert L.mk_attention_prefill(8, 1, 100, 16, 2, 96, 1920, 0, 1536, 1728, 1.0, 8, 1536, None) == 1  # seq % 128

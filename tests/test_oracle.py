@@ -81,3 +81,21 @@ def test_mirror_tracks_golden(preset, S):
         rng = (lg_g.max() - lg_g.min()).item()
         assert cos >= 0.999, cos
         assert (lg_g - lg_m[b]).abs().max().item() <= 2e-2 * rng
+
+
+def test_design_meets_accuracy_bar_1b_s1024():
+    """The numerics design (int8 weight-only, f32 residual stream, bf16 activations), evaluated by the
+    CPU mirror on the full 1B config at 1024 tokens, meets the accuracy bar against the FP32 golden."""
+    from oracle import mirror
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    cfg = PRESETS["minicpm5-1b"]
+    sd = random_state_dict(cfg, seed=1234)
+    pw = mk_weights.prepare_mk_weights(sd, cfg)
+    ids = synthetic_ids(1, 1024, seed=1234)
+    lg_m, _ = mirror.mirror_forward(ids, pw, cfg)
+    lg_g = golden.forward_logits(ids[0], golden.golden_weights(sd, cfg), cfg)
+    cos = torch.nn.functional.cosine_similarity(lg_g.double(), lg_m[0].double(), dim=0).item()
+    rng = (lg_g.max() - lg_g.min()).item()
+    assert cos >= 0.999
+    assert (lg_g - lg_m[0]).abs().max().item() <= 2e-2 * rng
+    assert golden.argmax_first(lg_g) == golden.argmax_first(lg_m[0])
