@@ -106,7 +106,19 @@ mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
-mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const int8_t* w, int M, int N, int K,
+// B operand: int8 [N, K] (K contiguous), box 64 (K) x 256 (N), no swizzle.
+mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GN)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
+}
+
+mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
                       int mode, const float* row_scale, const float* col_scale, void* out, int ldo, float resid,
                       cudaStream_t st, float* resid32 = nullptr, int ld_resid32 = 0) {
   GemmArgs ga;
@@ -115,7 +127,6 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const int8_t*
   ga.K = K;
   ga.mode = mode;
   ga.row_scale = row_scale;
-  ga.w = w;
   ga.col_scale = col_scale;
   ga.out = static_cast<__nv_bfloat16*>(out);
   ga.ldo = ldo;
@@ -125,7 +136,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const int8_t*
   ga.err = d->err;
   const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
-  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, ga);
+  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
   return cuda_status(cudaGetLastError());
 }
 
@@ -235,9 +246,8 @@ struct mk_handle {
   bool bound = false;
   mk_weight_ptrs w;
   int n_qkv = 0, q_dim = 0, kv_dim = 0;
-  std::vector<const int8_t*> w_qkv, w_o, w_gu, w_down;  // per-layer weight matrices
-  const int8_t* w_kv_last = nullptr;
-  const int8_t* w_q_last = nullptr;
+  std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_down;  // per layer
+  CUtensorMap m_kv_last, m_q_last;
 };
 
 extern "C" {
@@ -299,18 +309,19 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
   MK_CUDA(cudaSetDevice(h->device));
   const mk_config& c = h->cfg;
   const int L = c.num_layers, H = c.hidden, I = c.inter;
-  h->w_qkv.resize(L);
-  h->w_o.resize(L);
-  h->w_gu.resize(L);
-  h->w_down.resize(L);
+  h->m_qkv.resize(L);
+  h->m_o.resize(L);
+  h->m_gu.resize(L);
+  h->m_down.resize(L);
   for (int l = 0; l < L; ++l) {
-    h->w_qkv[l] = w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H;
-    h->w_o[l] = w->w_o + static_cast<size_t>(l) * H * h->q_dim;
-    h->w_gu[l] = w->w_gu + static_cast<size_t>(l) * 2 * I * H;
-    h->w_down[l] = w->w_down + static_cast<size_t>(l) * H * I;
+    MK_TRY(map_b(&h->m_qkv[l], w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H, h->n_qkv, H));
+    MK_TRY(map_b(&h->m_o[l], w->w_o + static_cast<size_t>(l) * H * h->q_dim, H, h->q_dim));
+    MK_TRY(map_b(&h->m_gu[l], w->w_gu + static_cast<size_t>(l) * 2 * I * H, 2 * I, H));
+    MK_TRY(map_b(&h->m_down[l], w->w_down + static_cast<size_t>(l) * H * I, H, I));
   }
-  h->w_q_last = h->w_qkv[L - 1];
-  h->w_kv_last = h->w_qkv[L - 1] + static_cast<size_t>(h->q_dim) * H;
+  const int8_t* wl = w->w_qkv + static_cast<size_t>(L - 1) * h->n_qkv * H;
+  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H));
+  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H, 2 * h->kv_dim, H));
   h->w = *w;
   h->bound = true;
   return MK_OK;
@@ -429,16 +440,16 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
 
   for (int l = 0; l < L - 1; ++l) {
     MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->w_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, rstd,
+    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, rstd,
                        h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st));
     MK_TRY(rope(qkv, T, nqkv, 0, c.n_q + c.n_kv, seq, 0));
     MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
-    MK_TRY(launch_gemm(d, mattn, h->w_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
+    MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
     MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->w_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, rstd,
+    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, rstd,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st));
-    MK_TRY(launch_gemm(d, mh, h->w_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
+    MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
   }
 
@@ -449,12 +460,12 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
     __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
     MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->w_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, rstd, sq + qd, kv, 2 * kvd, 0.f, st));
+    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, rstd, sq + qd, kv, 2 * kvd, 0.f, st));
     MK_TRY(rope(kv, T, 2 * kvd, 0, c.n_kv, seq, 0));
     mk::gather_last_kernel<<<bs, 256, 0, st>>>(x32, xl32, xlb, bs, seq, H);
     MK_CUDA(cudaGetLastError());
     MK_TRY(rms(xl32, bs, rstdl));
-    MK_TRY(launch_gemm(d, mxl, h->w_q_last, bs, qd, H, MK_GEMM_ROWSCALE, rstdl, sq, ql, qd, 0.f, st));
+    MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, rstdl, sq, ql, qd, 0.f, st));
     MK_TRY(rope(ql, bs, qd, 0, c.n_q, 1, seq - 1));
     AttnLastArgs la;
     la.S = seq;
@@ -471,12 +482,12 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
     mk::attn_last_kernel<<<dim3(c.n_q, bs), 256, smem, st>>>(ql, kv, al, la);
     MK_CUDA(cudaGetLastError());
-    MK_TRY(launch_gemm(d, mal, h->w_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
+    MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
     MK_TRY(rms(xl32, bs, rstdl));
-    MK_TRY(launch_gemm(d, mxl, h->w_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, rstdl,
+    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, rstdl,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st));
-    MK_TRY(launch_gemm(d, mhl, h->w_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
+    MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
   }
 
@@ -518,13 +529,13 @@ mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const 
   if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
   if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned16(resid32) || ld_resid32 % 4 || ld_resid32 < N))
     return resid32 ? MK_ERR_BAD_ALIGN : MK_ERR_BAD_ARG;
-  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(col_scale) || lda % 8 || ldo % 8 || lda < K)
-    return MK_ERR_BAD_ALIGN;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
-  CUtensorMap ma;
+  CUtensorMap ma, mb;
   MK_TRY(map_a(&ma, a, M, K, lda));
-  return launch_gemm(d, ma, w, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
+  MK_TRY(map_b(&mb, w, N, K));
+  return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
                      static_cast<cudaStream_t>(stream), resid32, ld_resid32);
 }
 

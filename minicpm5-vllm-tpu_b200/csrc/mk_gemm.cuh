@@ -19,11 +19,10 @@
 // (plugin/minicpm5_mk/mk_mlp.py:68-145).
 //
 // CTA layout (persistent, one CTA per SM, 14 warps):
-//   warp 0      : TMA producer (A tile 128x64 bf16 SW128)
+//   warp 0      : TMA producer (A tile 128x64 bf16 SW128, W tile 256x64 int8)
 //   warp 1      : TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=256, K=16)
 //   warps 2..5  : epilogue (TMEM -> registers -> global), one 32-lane TMEM quarter each
-//   warps 6..13 : int8 -> bf16 converters: int8 weight tile 256x64 from global (L2) into registers,
-//                 converted and stored as the 128B-swizzled K-major bf16 B tile
+//   warps 6..13 : int8 -> bf16 converters writing the 128B-swizzled K-major B tile
 // TMEM holds two 128x256 f32 accumulators (512 columns) so the epilogue of tile i overlaps the
 // main loop of tile i+1.
 #pragma once
@@ -37,13 +36,14 @@ enum GemmMode : int { GEMM_ROWSCALE = 0, GEMM_RESID = 1, GEMM_SWIGLU = 2, GEMM_C
 constexpr int GM = 128;   // rows of A per tile (UMMA M)
 constexpr int GN = 256;   // output channels per tile (UMMA N)
 constexpr int GK = 64;    // K per stage (one 128-byte swizzle row of bf16)
-constexpr int GSTAGES = 4;
+constexpr int GSTAGES = 3;
 constexpr int G_THREADS = 448;
 constexpr int G_CONV_WARP0 = 6;
 constexpr int G_CONV_WARPS = 8;
 constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 16 KB
+constexpr uint32_t G_BQ_BYTES = GN * GK;        // 16 KB
 constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 32 KB
-constexpr uint32_t G_STAGE_BYTES = G_A_BYTES + G_BH_BYTES;
+constexpr uint32_t G_STAGE_BYTES = G_A_BYTES + G_BQ_BYTES + G_BH_BYTES;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr size_t G_SMEM_BYTES = 1024 /*align pad*/ + GSTAGES * G_STAGE_BYTES + 256 /*barriers*/;
 
@@ -52,7 +52,6 @@ struct GemmArgs {
   int mode;
   const float* row_scale;  // [M] (ROWSCALE, SWIGLU)
   const float* col_scale;  // [N]
-  const int8_t* w;         // [N, K] int8 weights (read by the converter warps)
   __nv_bfloat16* out;      // [M, ldo]
   int ldo;
   float resid_scale;
@@ -62,12 +61,13 @@ struct GemmArgs {
 };
 
 __global__ void __launch_bounds__(G_THREADS, 1)
-    gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmA, const GemmArgs args) {
+    gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs args) {
   extern __shared__ uint8_t g_smem_raw[];
   const uint32_t raw = smem_u32(g_smem_raw);
   uint8_t* sbase = g_smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + GSTAGES * G_STAGE_BYTES);
-  uint64_t* full = bars;                 // [GSTAGES] TMA landed (A tile)
+  uint64_t* full = bars;                 // [GSTAGES] TMA landed (A + int8 W)
   uint64_t* conv = bars + GSTAGES;       // [GSTAGES] bf16 W tile written
   uint64_t* empty = bars + 2 * GSTAGES;  // [GSTAGES] MMAs reading the stage finished
   uint64_t* tfull = bars + 3 * GSTAGES;  // [2] accumulator ready
@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, G_TMEM_COLS);
@@ -115,12 +116,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t ph = 0;
       uint32_t issued = 0, issued_par = 0;  // per-stage: ever issued / parity of the last issue
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int mb = tile / num_n;
+        const int mb = tile / num_n, nb = tile % num_n;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) goto producer_done;
           uint8_t* st = sbase + s * G_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], G_A_BYTES);
+          mbar_arrive_expect_tx(&full[s], G_A_BYTES + G_BQ_BYTES);
           tma_load_2d(st, &tmA, &full[s], kt * GK, mb * GM);
+          tma_load_2d(st + G_A_BYTES, &tmB, &full[s], kt * GK, nb * GN);
           issued |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == GSTAGES) {
@@ -149,13 +151,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const uint32_t d = tmem_base + a * GN;
         bool ok = true;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&full[s], ph, abort_flag) || !mbar_wait(&conv[s], ph, abort_flag)) {
+          if (!mbar_wait(&conv[s], ph, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(sbase + s * G_STAGE_BYTES);
-          const uint32_t sb = sa + G_A_BYTES;
+          const uint32_t sb = sa + G_A_BYTES + G_BQ_BYTES;
           const uint64_t da = sdesc_kmajor_sw128(sa);
           const uint64_t db = sdesc_kmajor_sw128(sb);
 #pragma unroll
@@ -198,22 +200,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           tmem_ld_32x32b_x32(tbase + GN / 2 + c0, u);
           tmem_ld_wait();
           if (row_ok) {
-            const float4* sg = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-            const float4* su = reinterpret_cast<const float4*>(args.col_scale + n0 + GN / 2 + c0);
+            const float* sg = args.col_scale + n0 + c0;
+            const float* su = args.col_scale + n0 + GN / 2 + c0;
             uint32_t o[16];
 #pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 a4 = __ldg(sg + v), b4 = __ldg(su + v);
-              const float ga[4] = {a4.x, a4.y, a4.z, a4.w}, ub[4] = {b4.x, b4.y, b4.z, b4.w};
-              float hv[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float gg = __uint_as_float(g[4 * v + e]) * rs * ga[e];
-                const float uu = __uint_as_float(u[4 * v + e]) * rs * ub[e];
-                hv[e] = silu_f(gg) * uu;
-              }
-              o[2 * v] = pack_bf16x2(hv[0], hv[1]);
-              o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
+            for (int j = 0; j < 16; ++j) {
+              const float g0 = __uint_as_float(g[2 * j]) * rs * __ldg(sg + 2 * j);
+              const float g1 = __uint_as_float(g[2 * j + 1]) * rs * __ldg(sg + 2 * j + 1);
+              const float u0 = __uint_as_float(u[2 * j]) * rs * __ldg(su + 2 * j);
+              const float u1 = __uint_as_float(u[2 * j + 1]) * rs * __ldg(su + 2 * j + 1);
+              o[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
             }
             uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0);
 #pragma unroll
@@ -228,16 +224,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           tmem_ld_32x32b_x32(tbase + c0, acc);
           tmem_ld_wait();
           if (row_ok && n0 + c0 < args.N) {
-            const float4* sc4 = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-            float sc[32];
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 t4 = __ldg(sc4 + v);
-              sc[4 * v] = t4.x;
-              sc[4 * v + 1] = t4.y;
-              sc[4 * v + 2] = t4.z;
-              sc[4 * v + 3] = t4.w;
-            }
+            const float* sc = args.col_scale + n0 + c0;
             uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
             uint32_t o[16];
             if (args.mode == GEMM_RESID32) {
@@ -246,10 +233,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
               for (int v = 0; v < 8; ++v) {
                 float4 x = xr[v];
-                x.x += r * (__uint_as_float(acc[4 * v + 0]) * sc[4 * v + 0]);
-                x.y += r * (__uint_as_float(acc[4 * v + 1]) * sc[4 * v + 1]);
-                x.z += r * (__uint_as_float(acc[4 * v + 2]) * sc[4 * v + 2]);
-                x.w += r * (__uint_as_float(acc[4 * v + 3]) * sc[4 * v + 3]);
+                x.x += r * (__uint_as_float(acc[4 * v + 0]) * __ldg(sc + 4 * v + 0));
+                x.y += r * (__uint_as_float(acc[4 * v + 1]) * __ldg(sc + 4 * v + 1));
+                x.z += r * (__uint_as_float(acc[4 * v + 2]) * __ldg(sc + 4 * v + 2));
+                x.w += r * (__uint_as_float(acc[4 * v + 3]) * __ldg(sc + 4 * v + 3));
                 xr[v] = x;
                 o[2 * v] = pack_bf16x2(x.x, x.y);
                 o[2 * v + 1] = pack_bf16x2(x.z, x.w);
@@ -263,15 +250,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const float2 x = unpack_bf16x2(xw[j]);
-                const float y0 = x.x + r * (__uint_as_float(acc[2 * j]) * sc[2 * j]);
-                const float y1 = x.y + r * (__uint_as_float(acc[2 * j + 1]) * sc[2 * j + 1]);
+                const float y0 = x.x + r * (__uint_as_float(acc[2 * j]) * __ldg(sc + 2 * j));
+                const float y1 = x.y + r * (__uint_as_float(acc[2 * j + 1]) * __ldg(sc + 2 * j + 1));
                 o[j] = pack_bf16x2(y0, y1);
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * sc[2 * j],
-                                   __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1]);
+                o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * __ldg(sc + 2 * j),
+                                   __uint_as_float(acc[2 * j + 1]) * rs * __ldg(sc + 2 * j + 1));
             }
 #pragma unroll
             for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
@@ -284,64 +271,42 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
   } else {
     // -------------------------------------------------------------------- int8 -> bf16 converters
-    // Each thread owns 4 16-byte chunks of every 256 x 64 int8 weight tile: rows nrow0 + 64 i,
-    // bytes [16 kc, 16 kc + 16).  The chunks are read straight from global memory (L2-resident
-    // weights) three stages ahead into registers, so the int8 tile never passes through shared
-    // memory; only the bf16 result is stored (128B-swizzled K-major layout).
     const int ct = threadIdx.x - G_CONV_WARP0 * 32;  // 0..255
-    const int nrow0 = ct >> 2, kc = ct & 3;
-    const int my_tiles = (num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                         static_cast<int>(gridDim.x);
-    const int total = (static_cast<int>(blockIdx.x) < num_tiles) ? my_tiles * KT : 0;
-    auto load = [&](uint4 (&r)[4], int idx) {
-      if (idx >= total) return;
-      const int tile = blockIdx.x + (idx / KT) * gridDim.x;
-      const int nb = tile % num_n, kt = idx % KT;
-      const int8_t* base = args.w + kt * GK + kc * 16;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int n = nb * GN + nrow0 + 64 * i;
-        r[i] = n < args.N ? __ldg(reinterpret_cast<const uint4*>(base + static_cast<size_t>(n) * args.K))
-                          : make_uint4(0, 0, 0, 0);
-      }
-    };
-    uint4 r0[4], r1[4], r2[4];
-    load(r0, 0);
-    load(r1, 1);
-    load(r2, 2);
     int s = 0;
     uint32_t ph = 0;
-    for (int idx = 0; idx < total; ++idx) {
-      uint4 cur[4];
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&full[s], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* bq = sbase + s * G_STAGE_BYTES + G_A_BYTES;
+        uint8_t* bh = sbase + s * G_STAGE_BYTES + G_A_BYTES + G_BQ_BYTES;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        cur[i] = r0[i];
-        r0[i] = r1[i];
-        r1[i] = r2[i];
+        for (int i = 0; i < (GN * GK / 16) / (G_CONV_WARPS * 32); ++i) {
+          const int c = ct + i * G_CONV_WARPS * 32;  // 16-byte chunk of the int8 tile
+          const int n = c >> 2, kc = c & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(bq + n * GK + kc * 16);
+          uint4 o0, o1;
+          i8x4_to_bf16x4(v.x, o0.x, o0.y);
+          i8x4_to_bf16x4(v.y, o0.z, o0.w);
+          i8x4_to_bf16x4(v.z, o1.x, o1.y);
+          i8x4_to_bf16x4(v.w, o1.z, o1.w);
+          const int sw = n & 7;
+          uint8_t* rowp = bh + n * 128;
+          *reinterpret_cast<uint4*>(rowp + (((2 * kc) ^ sw) << 4)) = o0;
+          *reinterpret_cast<uint4*>(rowp + (((2 * kc + 1) ^ sw) << 4)) = o1;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+        if (++s == GSTAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
-      load(r2, idx + 3);
-      if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-      uint8_t* bh = sbase + s * G_STAGE_BYTES + G_A_BYTES;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int n = nrow0 + 64 * i;
-        uint4 o0, o1;
-        i8x4_to_bf16x4(cur[i].x, o0.x, o0.y);
-        i8x4_to_bf16x4(cur[i].y, o0.z, o0.w);
-        i8x4_to_bf16x4(cur[i].z, o1.x, o1.y);
-        i8x4_to_bf16x4(cur[i].w, o1.z, o1.w);
-        const int sw = n & 7;
-        uint8_t* rowp = bh + n * 128;
-        *reinterpret_cast<uint4*>(rowp + (((2 * kc) ^ sw) << 4)) = o0;
-        *reinterpret_cast<uint4*>(rowp + (((2 * kc + 1) ^ sw) << 4)) = o1;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
-      if (++s == GSTAGES) {
-        s = 0;
-        ph ^= 1u;
-      }
+      if (!ok) break;
     }
   }
 
