@@ -26,6 +26,9 @@ using mk::GemmArgs;
 __device__ int g_mk_err;
 
 constexpr int kMaxDevices = 64;
+// Weight-operand TMA box rows: 128 (half tile per CTA of a pair) with CTA pairs, 256 otherwise.
+constexpr bool kGemmPairs = true;
+constexpr int kWeightBoxRows = kGemmPairs ? 128 : 256;
 constexpr int kLmParts = 296;
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -69,6 +72,8 @@ mk_status device_state(DeviceState** out) {
     d.err = static_cast<int*>(p);
     MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::G_SMEM_BYTES)));
+    MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(mk::P_SMEM_BYTES)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::AttnShape<96>::SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -106,11 +111,11 @@ mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
-// B operand: int8 [N, K] (K contiguous), box 64 (K) x 256 (N), no swizzle.
-mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K) {
+// B operand: int8 [N, K] (K contiguous), box 64 (K) x box_rows (N), no swizzle.
+mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K, int box_rows = mk::GN) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GN)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -134,9 +139,16 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.resid32 = resid32;
   ga.ld_resid32 = ld_resid32;
   ga.err = d->err;
-  const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
-  const int grid = std::max(1, std::min(tiles, d->sm_count));
-  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+  if (kGemmPairs) {
+    // CTA pairs: the weight map's box covers the 128-row half tile each CTA stages.
+    const int tiles = ((M + mk::P_TILE_M - 1) / mk::P_TILE_M) * ((N + mk::GN - 1) / mk::GN);
+    const int clusters = std::max(1, std::min(tiles, d->sm_count / 2));
+    mk::gemm_w8a16_pair_kernel<<<2 * clusters, mk::G_THREADS, mk::P_SMEM_BYTES, st>>>(ma, mb, ga);
+  } else {
+    const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
+    const int grid = std::max(1, std::min(tiles, d->sm_count));
+    mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -314,14 +326,14 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
   h->m_gu.resize(L);
   h->m_down.resize(L);
   for (int l = 0; l < L; ++l) {
-    MK_TRY(map_b(&h->m_qkv[l], w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H, h->n_qkv, H));
-    MK_TRY(map_b(&h->m_o[l], w->w_o + static_cast<size_t>(l) * H * h->q_dim, H, h->q_dim));
-    MK_TRY(map_b(&h->m_gu[l], w->w_gu + static_cast<size_t>(l) * 2 * I * H, 2 * I, H));
-    MK_TRY(map_b(&h->m_down[l], w->w_down + static_cast<size_t>(l) * H * I, H, I));
+    MK_TRY(map_b(&h->m_qkv[l], w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H, h->n_qkv, H, kWeightBoxRows));
+    MK_TRY(map_b(&h->m_o[l], w->w_o + static_cast<size_t>(l) * H * h->q_dim, H, h->q_dim, kWeightBoxRows));
+    MK_TRY(map_b(&h->m_gu[l], w->w_gu + static_cast<size_t>(l) * 2 * I * H, 2 * I, H, kWeightBoxRows));
+    MK_TRY(map_b(&h->m_down[l], w->w_down + static_cast<size_t>(l) * H * I, H, I, kWeightBoxRows));
   }
   const int8_t* wl = w->w_qkv + static_cast<size_t>(L - 1) * h->n_qkv * H;
-  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H));
-  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H, 2 * h->kv_dim, H));
+  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H, kWeightBoxRows));
+  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H, 2 * h->kv_dim, H, kWeightBoxRows));
   h->w = *w;
   h->bound = true;
   return MK_OK;
@@ -534,7 +546,7 @@ mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const 
   MK_TRY(device_state(&d));
   CUtensorMap ma, mb;
   MK_TRY(map_a(&ma, a, M, K, lda));
-  MK_TRY(map_b(&mb, w, N, K));
+  MK_TRY(map_b(&mb, w, N, K, kWeightBoxRows));
   return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
                      static_cast<cudaStream_t>(stream), resid32, ld_resid32);
 }
