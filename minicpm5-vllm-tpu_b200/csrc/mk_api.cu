@@ -27,7 +27,10 @@ __device__ int g_mk_err;
 
 constexpr int kMaxDevices = 64;
 // Weight-operand TMA box rows: 128 (half tile per CTA of a pair) with CTA pairs, 256 otherwise.
-constexpr bool kGemmPairs = true;
+#ifndef MK_GEMM_PAIRS
+#define MK_GEMM_PAIRS 1
+#endif
+constexpr bool kGemmPairs = MK_GEMM_PAIRS != 0;
 constexpr int kWeightBoxRows = kGemmPairs ? 128 : 256;
 constexpr int kLmParts = 296;
 
