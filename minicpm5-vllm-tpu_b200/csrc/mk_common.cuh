@@ -341,16 +341,28 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) { return
 // ---------------------------------------------------------------------------------- numerics
 // Four signed int8 (one 32-bit word) -> four bf16 (two 32-bit words), exact.
 // Each byte is biased to u = x + 128 and placed in the mantissa of 2^23 (0x4B0000uu), so the f32
-// value is 2^23 + u; subtracting 2^23 + 128 leaves x exactly.  |x| <= 128 needs 8 significant bits,
-// so the upper 16 bits of the f32 are the exact bf16.
+// value is 2^23 + u; subtracting 2^23 + 128 (two lanes at a time with the packed f32x2 add) leaves x
+// exactly.  |x| <= 128 needs 8 significant bits, so the upper 16 bits of each f32 are the exact bf16.
 __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
-  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+  asm("{\n\t"
+      ".reg .b32 u, a0, a1, a2, a3;\n\t"
+      ".reg .b64 p0, p1;\n\t"
+      "xor.b32 u, %2, 0x80808080;\n\t"
+      "prmt.b32 a0, u, 0x4B000000, 0x7540;\n\t"
+      "prmt.b32 a1, u, 0x4B000000, 0x7541;\n\t"
+      "prmt.b32 a2, u, 0x4B000000, 0x7542;\n\t"
+      "prmt.b32 a3, u, 0x4B000000, 0x7543;\n\t"
+      "mov.b64 p0, {a0, a1};\n\t"
+      "mov.b64 p1, {a2, a3};\n\t"
+      "add.rn.f32x2 p0, p0, %3;\n\t"
+      "add.rn.f32x2 p1, p1, %3;\n\t"
+      "mov.b64 {a0, a1}, p0;\n\t"
+      "mov.b64 {a2, a3}, p1;\n\t"
+      "prmt.b32 %0, a0, a1, 0x7632;\n\t"
+      "prmt.b32 %1, a2, a3, 0x7632;\n\t"
+      "}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w), "l"(0xCB000080CB000080ull));  // (-(2^23 + 128), -(2^23 + 128)) as f32 pairs
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {

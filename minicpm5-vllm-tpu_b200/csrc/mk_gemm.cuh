@@ -333,7 +333,7 @@ constexpr uint32_t P_A_BYTES = 128 * GK * 2;    // 16 KB
 constexpr uint32_t P_BH_BYTES = 128 * GK * 2;   // 16 KB (bf16 half tile)
 constexpr uint32_t P_BQ_BYTES = 128 * GK;       // 8 KB  (int8 half tile)
 constexpr uint32_t P_STAGE_BYTES = P_A_BYTES + P_BH_BYTES + P_BQ_BYTES;
-constexpr size_t P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + 256;
+constexpr size_t P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + 512;
 constexpr int P_TILE_M = 256;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
@@ -344,11 +344,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
   uint8_t* sbase = p_smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + P_STAGES * P_STAGE_BYTES);
   uint64_t* full = bars;                  // [P_STAGES] local TMA landed (A + int8 W half)
-  uint64_t* conv = bars + P_STAGES;       // [P_STAGES] leader: bf16 halves of both CTAs written
+  uint64_t* conv = bars + P_STAGES;       // [P_STAGES] this CTA's bf16 half written (local arrivals)
   uint64_t* empty = bars + 2 * P_STAGES;  // [P_STAGES] pair MMAs reading the stage finished
   uint64_t* tfull = bars + 3 * P_STAGES;  // [2] accumulator ready (multicast)
   uint64_t* tempty = tfull + 2;           // [2] leader: both epilogues drained the accumulator
-  uint64_t* drain = tempty + 2;
+  uint64_t* conv_peer = tempty + 2;       // [P_STAGES] leader: the peer's bf16 half written (relayed)
+  uint64_t* drain = conv_peer + P_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -361,7 +362,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 2 * G_CONV_WARPS);
+      mbar_init(&conv[s], G_CONV_WARPS);
+      mbar_init(&conv_peer[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -429,7 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
         const uint32_t d = tmem_base + a * GN;
         bool ok = true;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait_cluster(&conv[s], ph, abort_flag)) {
+          if (!mbar_wait(&conv[s], ph, abort_flag) || !mbar_wait_cluster(&conv_peer[s], ph, abort_flag)) {
             ok = false;
             break;
           }
@@ -451,6 +453,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
       }
       mma_commit_pair(drain);
       mbar_wait_drain(drain, 0);
+    } else if (lane == 0 && cta == 1) {
+      // ------------------------------------------------------------------ relay (peer CTA)
+      // Forwards "this CTA's bf16 half of stage s is written" to the leader with one cluster-scope
+      // release per stage, so the converter warps only do CTA-local arrivals.
+      int s = 0;
+      uint32_t ph = 0;
+      const int my_tiles = (num_tiles - cid + ncl - 1) / ncl;
+      for (int idx = 0; idx < my_tiles * KT; ++idx) {
+        if (!mbar_wait(&conv[s], ph, abort_flag)) break;
+        mbar_arrive_remote(mapa_shared(smem_u32(&conv_peer[s]), 0));
+        if (++s == P_STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
     }
   } else if (warp < G_CONV_WARP0) {
     // -------------------------------------------------------------------- epilogue (own 128 rows)
@@ -590,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G_THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&conv[s]), 0));
+        if (lane == 0) mbar_arrive(&conv[s]);
         if (++s == P_STAGES) {
           s = 0;
           ph ^= 1u;
