@@ -26,12 +26,8 @@ using mk::GemmArgs;
 __device__ int g_mk_err;
 
 constexpr int kMaxDevices = 64;
-// Weight-operand TMA box rows: 128 (half tile per CTA of a pair) with CTA pairs, 256 otherwise.
-#ifndef MK_GEMM_PAIRS
-#define MK_GEMM_PAIRS 1
-#endif
-constexpr bool kGemmPairs = MK_GEMM_PAIRS != 0;
-constexpr int kWeightBoxRows = kGemmPairs ? 128 : 256;
+// Weight-operand TMA box rows (one int8 weight tile per k-step).
+constexpr int kWeightBoxRows = mk::GN;
 constexpr int kLmParts = 296;
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -75,8 +71,6 @@ mk_status device_state(DeviceState** out) {
     d.err = static_cast<int*>(p);
     MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::G_SMEM_BYTES)));
-    MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::P_SMEM_BYTES)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::AttnShape<96>::SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -142,16 +136,9 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.resid32 = resid32;
   ga.ld_resid32 = ld_resid32;
   ga.err = d->err;
-  if (kGemmPairs) {
-    // CTA pairs: the weight map's box covers the 128-row half tile each CTA stages.
-    const int tiles = ((M + mk::P_TILE_M - 1) / mk::P_TILE_M) * ((N + mk::GN - 1) / mk::GN);
-    const int clusters = std::max(1, std::min(tiles, d->sm_count / 2));
-    mk::gemm_w8a16_pair_kernel<<<2 * clusters, mk::G_THREADS, mk::P_SMEM_BYTES, st>>>(ma, mb, ga);
-  } else {
-    const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
-    const int grid = std::max(1, std::min(tiles, d->sm_count));
-    mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-  }
+  const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
+  const int grid = std::max(1, std::min(tiles, d->sm_count));
+  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
   return cuda_status(cudaGetLastError());
 }
 

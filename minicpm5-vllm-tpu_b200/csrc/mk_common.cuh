@@ -375,6 +375,6 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
   return __bfloat1622float2(v);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 }  // namespace mk
