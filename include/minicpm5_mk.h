@@ -54,7 +54,7 @@ typedef struct mk_config {
  *   rope_cos/sin   : f32  [max_seq, head_dim/2]
  *   w_qkv  int8 [L, (n_q+2 n_kv) head_dim, hidden]   s_qkv  f32 [L, (n_q+2 n_kv) head_dim]
  *   w_o    int8 [L, hidden, n_q head_dim]            s_o    f32 [L, hidden]
- *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows interleaved in blocks of 128)
+ *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows interleaved in blocks of 64)
  *                                                    s_gu   f32 [L, 2 inter]
  *   w_down int8 [L, hidden, inter]                   s_down f32 [L, hidden]
  * The Q rows carry 1/sqrt(head_dim); RMSNorm gains are folded into the weight columns. */
@@ -123,13 +123,13 @@ void mk_destroy(mk_handle* h);
 typedef enum mk_gemm_mode {
   MK_GEMM_ROWSCALE = 0, /* out = bf16(acc * row_scale[m] * col_scale[n])                     */
   MK_GEMM_RESID = 1,    /* out = bf16(out + resid_scale * acc * col_scale[n])   (in place)   */
-  MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g) * u) over 128-row gate/up blocks; out width N/2 */
+  MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g) * u) over 64-row gate/up blocks; out width N/2 */
   MK_GEMM_COLSCALE = 3, /* out = bf16(acc * col_scale[n])                                    */
   MK_GEMM_RESID32 = 4   /* resid32 += resid_scale * acc * col_scale[n] (f32, in place); out = bf16(resid32) */
 } mk_gemm_mode;
 
 /* W8A16 GEMM: acc[m, n] = sum_k a[m, k] * w[n, k]; a bf16 [M, lda], w int8 [N, K].
- * N % 128 == 0 (N % 256 == 0 for SWIGLU), K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
+ * N % 128 == 0, K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
  * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream.
  * Replaces `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` (mk_jax.py:233-269) and the
  * gate/up half of `fused_mlp` (mk_mlp.py:68-145). */

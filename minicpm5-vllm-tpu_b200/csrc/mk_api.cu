@@ -96,11 +96,11 @@ mk_status device_state(DeviceState** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// A operand: bf16 [rows, ld], box 64 (K) x 128 (rows), 128-byte swizzle.
+// A operand: bf16 [rows, ld], box 64 (K) x 256 (rows), 128-byte swizzle.
 mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GM)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GM)};  // 64 x 256
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -145,7 +145,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
 mk_status check_gemm_shape(int M, int N, int K, int mode) {
   if (M <= 0 || N <= 0 || K <= 0) return MK_ERR_BAD_SHAPE;
   if (N % 128 || K % mk::GK) return MK_ERR_BAD_SHAPE;
-  if (mode == MK_GEMM_SWIGLU && N % mk::GN) return MK_ERR_BAD_SHAPE;
+  if (mode == MK_GEMM_SWIGLU && N % mk::GN) return MK_ERR_BAD_SHAPE;  // 64 gate + 64 up per tile
   if (mode < 0 || mode > 4) return MK_ERR_BAD_ARG;
   return MK_OK;
 }

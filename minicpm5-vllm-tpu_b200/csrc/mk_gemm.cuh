@@ -11,7 +11,7 @@
 //   RESID32  : x32 = x32 + r * acc * s[n] (f32, in place), out = bf16(x32)
 //              o_proj / down + scaled residual on the f32 residual stream; `out` is the bf16 copy
 //              the next projection reads as its A operand
-//   SWIGLU   : tile = 128 gate + 128 up channels (interleaved weight rows);
+//   SWIGLU   : tile = 64 gate + 64 up channels (interleaved weight rows);
 //              h[m, i] = bf16(silu(g * rstd[m] * s_g) * (u * rstd[m] * s_u))   (out width N/2)
 //
 // Reference counterparts: `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` +
@@ -19,15 +19,18 @@
 // (plugin/minicpm5_mk/mk_mlp.py:68-145).
 //
 // CTA layout (persistent, one CTA per SM, 14 warps):
-//   warp 0 lane 0 : TMA producer of the A tiles (128 x 64 bf16, 128B swizzle), 4-slot ring
-//   warp 0 lane 1 : TMA producer of the int8 weight tiles (256 x 64), 4-slot ring that runs ahead
-//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=256, K=16)
+// Tile = 256 rows of A x 128 output channels: two M=128 UMMAs share one converted weight tile,
+// so every converted weight element feeds 256 rows.
+//   warp 0 lane 0 : TMA producer of the A tiles (256 x 64 bf16, 128B swizzle), 4-slot ring
+//   warp 0 lane 1 : TMA producer of the int8 weight tiles (128 x 64), 4-slot ring that runs ahead
+//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (2 x M=128, N=128, K=16)
 //   warps 2..5    : epilogue (TMEM -> registers -> global), one 32-lane TMEM quarter each; while a
 //                   tile's main loop runs they prefetch that tile's residual rows into L2
 //   warps 6..13   : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
 // The three rings are decoupled so the weight loads and their conversion run ahead of the MMAs and
 // only the A-tile load latency has to be covered by the A ring.  TMEM holds two 128x256 f32
-// accumulators (512 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+// accumulators (2 x 256 columns, each two 128x128 halves) so the epilogue of tile i overlaps the main
+// loop of tile i+1.
 #pragma once
 
 #include "mk_common.cuh"
@@ -36,8 +39,9 @@ namespace mk {
 
 enum GemmMode : int { GEMM_ROWSCALE = 0, GEMM_RESID = 1, GEMM_SWIGLU = 2, GEMM_COLSCALE = 3, GEMM_RESID32 = 4 };
 
-constexpr int GM = 128;   // rows of A per tile (UMMA M)
-constexpr int GN = 256;   // output channels per tile (UMMA N)
+constexpr int GM = 256;   // rows of A per tile: two UMMA M=128 halves sharing one converted weight tile
+constexpr int UM = 128;   // UMMA M
+constexpr int GN = 128;   // output channels per tile (UMMA N)
 constexpr int GK = 64;    // K per stage (one 128-byte swizzle row of bf16)
 constexpr int GA_SLOTS = 4;
 constexpr int GQ_SLOTS = 4;
@@ -45,9 +49,9 @@ constexpr int GH_SLOTS = 3;
 constexpr int G_THREADS = 448;
 constexpr int G_CONV_WARP0 = 6;
 constexpr int G_CONV_WARPS = 8;
-constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 16 KB
-constexpr uint32_t G_BQ_BYTES = GN * GK;        // 16 KB
-constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 32 KB
+constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 32 KB (two 16 KB halves)
+constexpr uint32_t G_BQ_BYTES = GN * GK;        // 8 KB
+constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 16 KB
 constexpr uint32_t G_RING_BYTES = GA_SLOTS * G_A_BYTES + GQ_SLOTS * G_BQ_BYTES + GH_SLOTS * G_BH_BYTES;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr size_t G_SMEM_BYTES = 1024 /*align pad*/ + G_RING_BYTES + 512 /*barriers*/;
@@ -76,9 +80,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   extern __shared__ uint8_t g_smem_raw[];
   const uint32_t raw = smem_u32(g_smem_raw);
   uint8_t* sbase = g_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sA = sbase;                                   // [GA_SLOTS] 16 KB
-  uint8_t* sH = sA + GA_SLOTS * G_A_BYTES;               // [GH_SLOTS] 32 KB (bf16 B)
-  uint8_t* sQ = sH + GH_SLOTS * G_BH_BYTES;              // [GQ_SLOTS] 16 KB (int8 B)
+  uint8_t* sA = sbase;                                   // [GA_SLOTS] 32 KB
+  uint8_t* sH = sA + GA_SLOTS * G_A_BYTES;               // [GH_SLOTS] 16 KB (bf16 B)
+  uint8_t* sQ = sH + GH_SLOTS * G_BH_BYTES;              // [GQ_SLOTS] 8 KB (int8 B)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + GQ_SLOTS * G_BQ_BYTES);
   uint64_t* a_full = bars;                   // [GA_SLOTS] TMA landed
   uint64_t* a_empty = a_full + GA_SLOTS;     // [GA_SLOTS] MMAs reading the slot finished
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = idesc_bf16_f32(GM, GN);
+      constexpr uint32_t idesc = idesc_bf16_f32(UM, GN);
       int idx = 0;
       bool ok = true;
       for (int it = 0; ok && it < my_tiles; ++it) {
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const uint32_t aph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[a], aph ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + a * GN;
+        const uint32_t d = tmem_base + a * 2 * GN;  // halves at +0 and +GN columns
         for (int kt = 0; kt < KT; ++kt, ++idx) {
           const int sa = idx % GA_SLOTS, sh = idx % GH_SLOTS;
           if (!mbar_wait(&a_full[sa], (idx / GA_SLOTS) & 1, abort_flag) ||
@@ -184,11 +188,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + sa * G_A_BYTES));
           const uint64_t db = sdesc_kmajor_sw128(smem_u32(sH + sh * G_BH_BYTES));
 #pragma unroll
-          for (int k = 0; k < GK / 16; ++k)
-            mma_f16_ss(d, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0 ? 1u : 0u);
+          for (int mi = 0; mi < GM / UM; ++mi) {
+            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + sa * G_A_BYTES + mi * (G_A_BYTES / 2)));
+#pragma unroll
+            for (int k = 0; k < GK / 16; ++k)
+              mma_f16_ss(d + mi * GN, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0 ? 1u : 0u);
+          }
           mma_commit(&a_empty[sa]);
           mma_commit(&h_empty[sh]);
         }
@@ -206,106 +213,117 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const int mb = tile / num_n, nb = tile % num_n;
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      const int row = mb * GM + q * 32 + lane;
-      const bool row_ok = row < args.M;
-      if (args.mode == GEMM_RESID32 && row_ok) {
-        // pull this tile's residual row segment (256 f32 = 1 KB) into L2 while the main loop runs
-        const char* xr = reinterpret_cast<const char*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 +
-                                                       nb * GN);
+      if (args.mode == GEMM_RESID32) {
+        // pull this tile's residual row segments (128 f32 = 512 B per row) into L2 while the main loop runs
 #pragma unroll
-        for (int l2 = 0; l2 < 8; ++l2) prefetch_l2(xr + l2 * 128);
+        for (int mi = 0; mi < GM / UM; ++mi) {
+          const int row = mb * GM + mi * UM + q * 32 + lane;
+          if (row < args.M) {
+            const char* xr = reinterpret_cast<const char*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 +
+                                                           nb * GN);
+#pragma unroll
+            for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
+          }
+        }
       }
       if (!mbar_wait(&tfull[a], aph, abort_flag)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + a * GN + (static_cast<uint32_t>(q * 32) << 16);
-      float rs = 1.0f;
-      if ((args.mode == GEMM_ROWSCALE || args.mode == GEMM_SWIGLU) && row_ok) rs = __ldg(args.row_scale + row);
-      if (args.mode == GEMM_SWIGLU) {
-        const int n0 = nb * GN;           // weight rows: [n0, n0+128) gate, [n0+128, n0+256) up
-        const int i0 = nb * (GN / 2);     // output channels
 #pragma unroll 1
-        for (int c0 = 0; c0 < GN / 2; c0 += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(tbase + c0, g);
-          tmem_ld_32x32b_x32(tbase + GN / 2 + c0, u);
-          tmem_ld_wait();
-          if (row_ok) {
-            const float4* sg = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-            const float4* su = reinterpret_cast<const float4*>(args.col_scale + n0 + GN / 2 + c0);
-            uint32_t o[16];
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 a4 = __ldg(sg + v), b4 = __ldg(su + v);
-              const float ga[4] = {a4.x, a4.y, a4.z, a4.w}, ub[4] = {b4.x, b4.y, b4.z, b4.w};
-              float hv[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                hv[e] = silu_f(__uint_as_float(g[4 * v + e]) * rs * ga[e]) * (__uint_as_float(u[4 * v + e]) * rs * ub[e]);
-              o[2 * v] = pack_bf16x2(hv[0], hv[1]);
-              o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-          }
-        }
-      } else {
-        const int n0 = nb * GN;
+      for (int mi = 0; mi < GM / UM; ++mi) {
+        const int row = mb * GM + mi * UM + q * 32 + lane;
+        const bool row_ok = row < args.M;
+        const uint32_t tbase = tmem_base + a * 2 * GN + mi * GN + (static_cast<uint32_t>(q * 32) << 16);
+        float rs = 1.0f;
+        if ((args.mode == GEMM_ROWSCALE || args.mode == GEMM_SWIGLU) && row_ok) rs = __ldg(args.row_scale + row);
+        if (args.mode == GEMM_SWIGLU) {
+          const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
+          const int i0 = nb * (GN / 2);     // output channels
 #pragma unroll 1
-        for (int c0 = 0; c0 < GN; c0 += 32) {
-          uint32_t acc[32];
-          tmem_ld_32x32b_x32(tbase + c0, acc);
-          tmem_ld_wait();
-          if (row_ok && n0 + c0 < args.N) {
-            const float4* sc4 = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-            float sc[32];
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 t4 = __ldg(sc4 + v);
-              sc[4 * v] = t4.x;
-              sc[4 * v + 1] = t4.y;
-              sc[4 * v + 2] = t4.z;
-              sc[4 * v + 3] = t4.w;
-            }
-            uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
-            uint32_t o[16];
-            if (args.mode == GEMM_RESID32) {
-              float4* xr = reinterpret_cast<float4*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0);
-              const float r = args.resid_scale;
-              float4 xv[8];
-#pragma unroll
-              for (int v = 0; v < 8; ++v) xv[v] = xr[v];
+          for (int c0 = 0; c0 < GN / 2; c0 += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(tbase + c0, g);
+            tmem_ld_32x32b_x32(tbase + GN / 2 + c0, u);
+            tmem_ld_wait();
+            if (row_ok) {
+              const float4* sg = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
+              const float4* su = reinterpret_cast<const float4*>(args.col_scale + n0 + GN / 2 + c0);
+              uint32_t o[16];
 #pragma unroll
               for (int v = 0; v < 8; ++v) {
-                float4 x = xv[v];
-                x.x += r * (__uint_as_float(acc[4 * v + 0]) * sc[4 * v + 0]);
-                x.y += r * (__uint_as_float(acc[4 * v + 1]) * sc[4 * v + 1]);
-                x.z += r * (__uint_as_float(acc[4 * v + 2]) * sc[4 * v + 2]);
-                x.w += r * (__uint_as_float(acc[4 * v + 3]) * sc[4 * v + 3]);
-                xr[v] = x;
-                o[2 * v] = pack_bf16x2(x.x, x.y);
-                o[2 * v + 1] = pack_bf16x2(x.z, x.w);
+                const float4 a4 = __ldg(sg + v), b4 = __ldg(su + v);
+                const float ga[4] = {a4.x, a4.y, a4.z, a4.w}, ub[4] = {b4.x, b4.y, b4.z, b4.w};
+                float hv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  hv[e] = silu_f(__uint_as_float(g[4 * v + e]) * rs * ga[e]) *
+                          (__uint_as_float(u[4 * v + e]) * rs * ub[e]);
+                o[2 * v] = pack_bf16x2(hv[0], hv[1]);
+                o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
               }
-            } else if (args.mode == GEMM_RESID) {
-              uint4 xin[4];
+              uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0);
 #pragma unroll
-              for (int v = 0; v < 4; ++v) xin[v] = dst[v];
-              const uint32_t* xw = reinterpret_cast<const uint32_t*>(xin);
-              const float r = args.resid_scale;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float2 x = unpack_bf16x2(xw[j]);
-                o[j] = pack_bf16x2(x.x + r * (__uint_as_float(acc[2 * j]) * sc[2 * j]),
-                                   x.y + r * (__uint_as_float(acc[2 * j + 1]) * sc[2 * j + 1]));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * sc[2 * j],
-                                   __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1]);
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
             }
+          }
+        } else {
+          const int n0 = nb * GN;
+#pragma unroll 1
+          for (int c0 = 0; c0 < GN; c0 += 32) {
+            uint32_t acc[32];
+            tmem_ld_32x32b_x32(tbase + c0, acc);
+            tmem_ld_wait();
+            if (row_ok && n0 + c0 < args.N) {
+              const float4* sc4 = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
+              float sc[32];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              for (int v = 0; v < 8; ++v) {
+                const float4 t4 = __ldg(sc4 + v);
+                sc[4 * v] = t4.x;
+                sc[4 * v + 1] = t4.y;
+                sc[4 * v + 2] = t4.z;
+                sc[4 * v + 3] = t4.w;
+              }
+              uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
+              uint32_t o[16];
+              if (args.mode == GEMM_RESID32) {
+                float4* xr =
+                    reinterpret_cast<float4*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0);
+                const float r = args.resid_scale;
+                float4 xv[8];
+#pragma unroll
+                for (int v = 0; v < 8; ++v) xv[v] = xr[v];
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                  float4 x = xv[v];
+                  x.x += r * (__uint_as_float(acc[4 * v + 0]) * sc[4 * v + 0]);
+                  x.y += r * (__uint_as_float(acc[4 * v + 1]) * sc[4 * v + 1]);
+                  x.z += r * (__uint_as_float(acc[4 * v + 2]) * sc[4 * v + 2]);
+                  x.w += r * (__uint_as_float(acc[4 * v + 3]) * sc[4 * v + 3]);
+                  xr[v] = x;
+                  o[2 * v] = pack_bf16x2(x.x, x.y);
+                  o[2 * v + 1] = pack_bf16x2(x.z, x.w);
+                }
+              } else if (args.mode == GEMM_RESID) {
+                uint4 xin[4];
+#pragma unroll
+                for (int v = 0; v < 4; ++v) xin[v] = dst[v];
+                const uint32_t* xw = reinterpret_cast<const uint32_t*>(xin);
+                const float r = args.resid_scale;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float2 x = unpack_bf16x2(xw[j]);
+                  o[j] = pack_bf16x2(x.x + r * (__uint_as_float(acc[2 * j]) * sc[2 * j]),
+                                     x.y + r * (__uint_as_float(acc[2 * j + 1]) * sc[2 * j + 1]));
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * sc[2 * j],
+                                     __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1]);
+              }
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
           }
         }
       }

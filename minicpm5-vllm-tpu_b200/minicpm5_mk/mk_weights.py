@@ -11,7 +11,7 @@ the parts this path keeps, re-laid-out for the tcgen05 GEMMs:
   No activation quantisation (the reference's W8A8 SmoothQuant calibration is not used).
 * Every projection stays [out_features, in_features] (K contiguous = "K-major" B operand).
 * gate/up are fused into one [2I, H] matrix interleaved in blocks of GU_BLOCK rows
-  ([g_0..g_127, u_0..u_127, g_128..g_255, u_128..]) so each 256-row GEMM tile holds matching gate and
+  ([g_0..g_63, u_0..u_63, g_64..g_127, u_64..]) so each 128-row GEMM tile holds matching gate and
   up channels and SiLU(g)*u is tile-local in the epilogue (same idea as the reference's
   chunk-interleaved `interleave_gu`, `plugin/minicpm5_mk/mk_mlp.py:148-158`).
 * All L layers are int8 (the reference keeps its last layer in bf16 because W8A8 hurt accuracy;
@@ -30,7 +30,7 @@ import torch
 
 from .mk_config import MkConfig
 
-GU_BLOCK = 128
+GU_BLOCK = 64
 BF16 = torch.bfloat16
 F32 = torch.float32
 

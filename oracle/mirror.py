@@ -41,7 +41,7 @@ def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor
     return bf(torch.cat([a * c - b * s, b * c + a * s], dim=-1))
 
 
-def _deinterleave(t: torch.Tensor, block: int = 128):
+def _deinterleave(t: torch.Tensor, block: int = 64):
     n2 = t.shape[0]
     v = t.reshape(n2 // (2 * block), 2, block, *t.shape[1:])
     return v[:, 0].reshape(n2 // 2, *t.shape[1:]), v[:, 1].reshape(n2 // 2, *t.shape[1:])

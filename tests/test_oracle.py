@@ -51,7 +51,7 @@ def test_gu_interleave_roundtrip():
     g = torch.arange(512 * 3).reshape(512, 3)
     u = -g
     x = mk_weights.interleave_gu(g, u)
-    assert torch.equal(x[:128], g[:128]) and torch.equal(x[128:256], u[:128])
+    assert torch.equal(x[:64], g[:64]) and torch.equal(x[64:128], u[:64])
     g2, u2 = mk_weights.deinterleave_gu(x)
     assert torch.equal(g2, g) and torch.equal(u2, u)
 
