@@ -49,7 +49,7 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
-    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_down", "attn"],
+    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_down", "attn"],
                     help="time one isolated kernel of the forward (profiling driver) instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
     ap.add_argument("--kernel-iters", type=int, default=3)
@@ -70,12 +70,15 @@ def run_kernel(a):
     H, I = cfg.hidden, cfg.inter
     if a.kernel.startswith("gemm"):
         N, K, mode = {"gemm_swiglu": (2 * I, H, _lib.MK_GEMM_SWIGLU), "gemm_qkv": (cfg.qkv_dim, H, _lib.MK_GEMM_ROWSCALE),
-                      "gemm_down": (H, I, _lib.MK_GEMM_RESID)}[a.kernel]
+                      "gemm_o": (H, cfg.q_dim, _lib.MK_GEMM_RESID32),
+                      "gemm_down": (H, I, _lib.MK_GEMM_RESID32)}[a.kernel]
         x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
         w8, s = quantize_per_out_channel(torch.randn((N, K), generator=g, device=dev) * 0.02)
         rstd = torch.ones((T,), device=dev)
         out = torch.zeros((T, N // 2 if mode == _lib.MK_GEMM_SWIGLU else N), dtype=torch.bfloat16, device=dev)
-        fn = lambda: ops.gemm_w8a16(x, w8, s, mode, row_scale=rstd, resid_scale=0.3, out=out)  # noqa: E731
+        x32 = torch.zeros((T, N), dtype=torch.float32, device=dev) if mode == _lib.MK_GEMM_RESID32 else None
+        fn = lambda: ops.gemm_w8a16(x, w8, s, mode, row_scale=rstd, resid_scale=0.3, out=out,  # noqa: E731
+                                    resid32=x32)
         flops = 2.0 * T * N * K
     else:
         qkv = torch.randn((T, cfg.qkv_dim), generator=g, device=dev).to(torch.bfloat16)

@@ -230,10 +230,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         for (int e = 0; e < 64; ++e)
           if (e >= valid) v[e] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row max: four independent partial maxima (no 64-long dependency chain)
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
-      const float m_tile = mx * sc;
+      for (int e = 0; e < 64; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+      const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
       const bool need = m_tile > m_used + TA_RESCALE_THRESHOLD;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O_t += P_t V of the previous tile must have landed before O_t is rescaled
@@ -257,13 +258,15 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       }
       if (need) m_used = m_tile;
       uint32_t pk[32];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sc, -m_used));
         const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sc, -m_used));
-        l += p0 + p1;
+        ls[e & 3] += p0 + p1;
         pk[e] = pack_bf16x2(p0, p1);
       }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_st_32x32b_x32(tS + b * 64, pk);  // P_t(j) over the S columns just read
       tmem_st_wait();
       tc_fence_before();
