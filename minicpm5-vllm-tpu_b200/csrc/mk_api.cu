@@ -120,9 +120,20 @@ mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K, int box_rows = mk
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
+// Optional fused epilogue work of one GEMM launch (RMSNorm statistics, RoPE).
+struct GemmFusion {
+  float* rowsq = nullptr;  // per-(row, 128-column tile) sums of squares of the f32 residual
+  int rowsq_ld = 0, rowsq_np = 0;
+  float inv_norm_dim = 0.f, eps = 0.f;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_cols = 0, head_dim = 0, rope_seq = 1, rope_pos_base = 0;
+};
+
 mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
                       int mode, const float* row_scale, const float* col_scale, void* out, int ldo, float resid,
-                      cudaStream_t st, float* resid32 = nullptr, int ld_resid32 = 0) {
+                      cudaStream_t st, float* resid32 = nullptr, int ld_resid32 = 0,
+                      const GemmFusion& fu = GemmFusion()) {
   GemmArgs ga;
   ga.M = M;
   ga.N = N;
@@ -135,6 +146,17 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.resid_scale = resid;
   ga.resid32 = resid32;
   ga.ld_resid32 = ld_resid32;
+  ga.rowsq = fu.rowsq;
+  ga.rowsq_ld = fu.rowsq_ld;
+  ga.rowsq_np = fu.rowsq_np;
+  ga.inv_norm_dim = fu.inv_norm_dim;
+  ga.eps = fu.eps;
+  ga.rope_cos = fu.rope_cos;
+  ga.rope_sin = fu.rope_sin;
+  ga.rope_cols = fu.rope_cols;
+  ga.head_dim = fu.head_dim > 0 ? fu.head_dim : 1;
+  ga.rope_seq = fu.rope_seq > 0 ? fu.rope_seq : 1;
+  ga.rope_pos_base = fu.rope_pos_base;
   ga.err = d->err;
   const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
@@ -331,7 +353,7 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
 
 namespace {
 struct Workspace {
-  size_t x32, xb, qkv, attn, hbuf, rstd, xl32, xlb, ql, al, hl, rstdl, hf, logits, pval, pidx, top1, total;
+  size_t x32, xb, qkv, attn, hbuf, rowsq, xl32, xlb, ql, al, hl, rowsql, hf, logits, pval, pidx, top1, total;
 };
 
 Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
@@ -349,13 +371,13 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
   w.qkv = take(T * h->n_qkv * 2);
   w.attn = take(T * h->q_dim * 2);
   w.hbuf = take(T * c.inter * 2);
-  w.rstd = take(T * 4);
+  w.rowsq = take(T * (c.hidden / 128) * 4);
   w.xl32 = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.xlb = take(static_cast<size_t>(bs) * c.hidden * 2);
   w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
-  w.rstdl = take(static_cast<size_t>(bs) * 4);
+  w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 128) * 4);
   w.hf = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.logits = take(static_cast<size_t>(bs) * c.vocab * 4);
   w.pval = take(static_cast<size_t>(bs) * kLmParts * 4);
@@ -410,7 +432,7 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   float *x32 = f32(ws.x32), *xl32 = f32(ws.xl32);
   __nv_bfloat16 *xb = bf(ws.xb), *qkv = bf(ws.qkv), *attn = bf(ws.attn), *hb = bf(ws.hbuf);
   __nv_bfloat16 *xlb = bf(ws.xlb), *ql = bf(ws.ql), *al = bf(ws.al), *hl = bf(ws.hl);
-  float *rstd = f32(ws.rstd), *rstdl = f32(ws.rstdl), *hf = f32(ws.hf);
+  float *rowsq = f32(ws.rowsq), *rowsql = f32(ws.rowsql), *hf = f32(ws.hf);
   float* logits = d_logits ? d_logits : f32(ws.logits);
   int32_t* top1 = d_top1 ? d_top1 : reinterpret_cast<int32_t*>(base + ws.top1);
   const float r = c.residual_scale;
@@ -424,35 +446,49 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   MK_TRY(map_a(&mhl, hl, bs, I, I));
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
+  const int np = H / 128;       // 128-column tiles of the residual: RMSNorm partial sums per row
   mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
-      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err);
+      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err, rowsq, np);
   MK_CUDA(cudaGetLastError());
 
-  auto rms = [&](const float* src, int rows, float* dst) -> mk_status {
-    mk::rms_rstd_kernel<<<(rows + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(src, dst, rows, H, H, c.eps);
-    return cuda_status(cudaGetLastError());
+  // RMSNorm folded into the projections: rstd comes from the residual's per-tile sums of squares
+  // (written by the embedding and by every residual-update epilogue).
+  auto norm_from = [&](float* sq) {
+    GemmFusion f;
+    f.rowsq = sq;
+    f.rowsq_ld = np;
+    f.rowsq_np = np;
+    f.inv_norm_dim = 1.0f / static_cast<float>(H);
+    f.eps = c.eps;
+    return f;
   };
-  auto rope = [&](__nv_bfloat16* buf, int rows, int ld, int col0, int nh, int sq, int pos_base) -> mk_status {
-    const size_t work = static_cast<size_t>(rows) * nh * (hd / 4);
-    const int blocks = static_cast<int>(std::min<size_t>((work + 255) / 256, static_cast<size_t>(d->sm_count) * 16));
-    mk::rope_kernel<<<std::max(blocks, 1), 256, 0, st>>>(buf, h->w.rope_cos, h->w.rope_sin, rows, ld, col0, nh, hd,
-                                                        sq, pos_base);
-    return cuda_status(cudaGetLastError());
+  auto with_rope = [&](GemmFusion f, int cols, int sq, int pos_base) {
+    f.rope_cos = h->w.rope_cos;
+    f.rope_sin = h->w.rope_sin;
+    f.rope_cols = cols;
+    f.head_dim = hd;
+    f.rope_seq = sq;
+    f.rope_pos_base = pos_base;
+    return f;
   };
+  GemmFusion resid_stats;  // residual epilogues write the statistics
+  resid_stats.rowsq = rowsq;
+  resid_stats.rowsq_ld = np;
+  GemmFusion resid_stats_last = resid_stats;
+  resid_stats_last.rowsq = rowsql;
 
   for (int l = 0; l < L - 1; ++l) {
-    MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, rstd,
-                       h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st));
-    MK_TRY(rope(qkv, T, nqkv, 0, c.n_q + c.n_kv, seq, 0));
+    // QKV projection with RMSNorm and RoPE (Q/K) fused into the epilogue
+    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
+                       h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st, nullptr, 0,
+                       with_rope(norm_from(rowsq), qd + kvd, seq, 0)));
     MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
     MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
-                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
-    MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, rstd,
-                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st));
+                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0, norm_from(rowsq)));
     MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H));
+                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
   }
 
   // Last layer: K/V for every position, everything else for the last position only
@@ -461,14 +497,12 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     const int l = L - 1;
     const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
     __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
-    MK_TRY(rms(x32, T, rstd));
-    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, rstd, sq + qd, kv, 2 * kvd, 0.f, st));
-    MK_TRY(rope(kv, T, 2 * kvd, 0, c.n_kv, seq, 0));
-    mk::gather_last_kernel<<<bs, 256, 0, st>>>(x32, xl32, xlb, bs, seq, H);
+    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
+                       nullptr, 0, with_rope(norm_from(rowsq), kvd, seq, 0)));
+    mk::gather_last_kernel<<<bs, 256, 0, st>>>(x32, xl32, xlb, bs, seq, H, rowsq, rowsql, np);
     MK_CUDA(cudaGetLastError());
-    MK_TRY(rms(xl32, bs, rstdl));
-    MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, rstdl, sq, ql, qd, 0.f, st));
-    MK_TRY(rope(ql, bs, qd, 0, c.n_q, 1, seq - 1));
+    MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, nullptr, sq, ql, qd, 0.f, st, nullptr, 0,
+                       with_rope(norm_from(rowsql), qd, 1, seq - 1)));
     AttnLastArgs la;
     la.S = seq;
     la.n_q = c.n_q;
@@ -485,12 +519,11 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     mk::attn_last_kernel<<<dim3(c.n_q, bs), 256, smem, st>>>(ql, kv, al, la);
     MK_CUDA(cudaGetLastError());
     MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
-                       h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
-    MK_TRY(rms(xl32, bs, rstdl));
-    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, rstdl,
-                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st));
+                       h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
+    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H));
+                       h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
   }
 
   mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
@@ -502,8 +535,8 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
 
 int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq) {
   if (!h || bs <= 0 || seq <= 0) return 0;
-  const int per_layer = 8;   // rms, qkv gemm, rope, attention, o gemm, rms, gate/up gemm, down gemm
-  const int last_layer = 12; // rms, kv gemm, rope, gather, rms, q gemm, rope, attention, o, rms, gate/up, down
+  const int per_layer = 5;  // qkv gemm (+RMSNorm, RoPE), attention, o gemm, gate/up gemm, down gemm
+  const int last_layer = 7; // kv gemm, gather, q gemm, attention, o gemm, gate/up gemm, down gemm
   return 1 + (h->cfg.num_layers - 1) * per_layer + last_layer + 1 + (bs + mk::LM_ROWS - 1) / mk::LM_ROWS + 1;
 }
 

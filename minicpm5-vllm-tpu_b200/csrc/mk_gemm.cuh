@@ -6,7 +6,8 @@
 //                                                           channel scale s[n], f32)
 // Epilogue modes (the per-row / per-column scalings commute with the sum, so they are applied to
 // the f32 accumulator read back from TMEM):
-//   ROWSCALE : out = bf16(acc * rstd[m] * s[n])                   RMSNorm-fused projections (QKV)
+//   ROWSCALE : out = bf16(acc * rstd[m] * s[n])                   RMSNorm-fused projections (QKV),
+//              optionally with RoPE applied to the Q/K columns before the bf16 rounding
 //   RESID    : out = bf16(out + r * acc * s[n])   (in place)       bf16 residual
 //   RESID32  : x32 = x32 + r * acc * s[n] (f32, in place), out = bf16(x32)
 //              o_proj / down + scaled residual on the f32 residual stream; `out` is the bf16 copy
@@ -67,6 +68,18 @@ struct GemmArgs {
   float resid_scale;
   float* resid32;          // [M, ld_resid32] (RESID32)
   int ld_resid32;
+  // Fused RMSNorm statistics.  RESID32 writes, per row and 128-column tile, the sum of squares of
+  // the updated residual into rowsq[row * rowsq_ld + tile].  ROWSCALE / SWIGLU with rowsq != null
+  // take rstd = rsqrt(sum over rowsq_np partials / norm_dim + eps) instead of row_scale.
+  float* rowsq;
+  int rowsq_ld, rowsq_np;
+  float inv_norm_dim, eps;
+  // Fused RoPE (ROWSCALE): columns [0, rope_cols) hold heads of width head_dim whose rotation pairs
+  // (i, i + head_dim/2) are stored interleaved as adjacent columns (2j, 2j + 1); position of row m
+  // is rope_pos_base + m % rope_seq; tables f32 [max_seq, head_dim/2].
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_cols, head_dim, rope_seq, rope_pos_base;
   int* err;
 };
 
@@ -234,7 +247,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const bool row_ok = row < args.M;
         const uint32_t tbase = tmem_base + a * 2 * GN + mi * GN + (static_cast<uint32_t>(q * 32) << 16);
         float rs = 1.0f;
-        if ((args.mode == GEMM_ROWSCALE || args.mode == GEMM_SWIGLU) && row_ok) rs = __ldg(args.row_scale + row);
+        if ((args.mode == GEMM_ROWSCALE || args.mode == GEMM_SWIGLU) && row_ok) {
+          if (args.rowsq) {
+            const float* ps = args.rowsq + static_cast<size_t>(row) * args.rowsq_ld;
+            float ss = 0.f;
+            for (int p = 0; p < args.rowsq_np; ++p) ss += ps[p];
+            rs = rsqrtf(ss * args.inv_norm_dim + args.eps);
+          } else {
+            rs = __ldg(args.row_scale + row);
+          }
+        }
+        float sumsq = 0.f;  // RESID32: sum of squares of this row's updated 128-column segment
         if (args.mode == GEMM_SWIGLU) {
           const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
           const int i0 = nb * (GN / 2);     // output channels
@@ -300,6 +323,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                   x.z += r * (__uint_as_float(acc[4 * v + 2]) * sc[4 * v + 2]);
                   x.w += r * (__uint_as_float(acc[4 * v + 3]) * sc[4 * v + 3]);
                   xr[v] = x;
+                  sumsq += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
                   o[2 * v] = pack_bf16x2(x.x, x.y);
                   o[2 * v + 1] = pack_bf16x2(x.z, x.w);
                 }
@@ -315,6 +339,19 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                   o[j] = pack_bf16x2(x.x + r * (__uint_as_float(acc[2 * j]) * sc[2 * j]),
                                      x.y + r * (__uint_as_float(acc[2 * j + 1]) * sc[2 * j + 1]));
                 }
+              } else if (n0 + c0 < args.rope_cols) {
+                // projection + RoPE on adjacent (x_j, x_{j+hd/2}) pairs, rounded to bf16 once
+                const int pos = args.rope_pos_base + row % args.rope_seq;
+                const float* ct = args.rope_cos + static_cast<size_t>(pos) * (args.head_dim >> 1);
+                const float* st = args.rope_sin + static_cast<size_t>(pos) * (args.head_dim >> 1);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int pj = ((n0 + c0 + 2 * j) % args.head_dim) >> 1;
+                  const float c = __ldg(ct + pj), sn = __ldg(st + pj);
+                  const float xa = __uint_as_float(acc[2 * j]) * rs * sc[2 * j];
+                  const float xb = __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1];
+                  o[j] = pack_bf16x2(xa * c - xb * sn, xb * c + xa * sn);
+                }
               } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -325,6 +362,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
             }
           }
+          if (args.mode == GEMM_RESID32 && args.rowsq && row_ok)
+            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + nb] = sumsq;
         }
       }
       tc_fence_before();

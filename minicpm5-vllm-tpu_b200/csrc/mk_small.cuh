@@ -12,13 +12,15 @@ namespace mk {
 // DEV_ERR_BAD_TOKEN_ID.
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
                              float* __restrict__ x32, __nv_bfloat16* __restrict__ xb, int T, int H, int V, float scale,
-                             int* err) {
+                             int* err, float* __restrict__ rowsq = nullptr, int rowsq_ld = 0) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const int id = ids[row];
   uint4* db = reinterpret_cast<uint4*>(xb + static_cast<size_t>(row) * H);
   float4* d32 = reinterpret_cast<float4*>(x32 + static_cast<size_t>(row) * H);
+  if (rowsq)  // fused RMSNorm statistics: the whole row's sum of squares in slot 0, other slots 0
+    for (int p = lane; p < rowsq_ld; p += 32) rowsq[static_cast<size_t>(row) * rowsq_ld + p] = 0.f;
   if (id < 0 || id >= V) {
     if (lane == 0 && err) atomicCAS(err, 0, DEV_ERR_BAD_TOKEN_ID);
     for (int c = lane; c < H / 8; c += 32) {
@@ -29,6 +31,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat1
     return;
   }
   const uint4* src = reinterpret_cast<const uint4*>(E + static_cast<size_t>(id) * H);
+  float ss = 0.f;
   for (int c = lane; c < H / 8; c += 32) {
     uint4 v = __ldg(src + c);
     uint32_t* w = reinterpret_cast<uint32_t*>(&v);
@@ -43,6 +46,13 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat1
     db[c] = v;
     d32[2 * c] = make_float4(f[0], f[1], f[2], f[3]);
     d32[2 * c + 1] = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+  }
+  if (rowsq) {
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+    __syncwarp();
+    if (lane == 0) rowsq[static_cast<size_t>(row) * rowsq_ld] = ss;
   }
 }
 
@@ -93,14 +103,20 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, const float* __restri
 
 // xl32[b, :] = x32[b*S + S-1, :], xlb = bf16 copy (the rows the last layer's token-local work needs).
 __global__ void gather_last_kernel(const float* __restrict__ x32, float* __restrict__ xl32,
-                                   __nv_bfloat16* __restrict__ xlb, int bs, int S, int H) {
+                                   __nv_bfloat16* __restrict__ xlb, int bs, int S, int H,
+                                   const float* __restrict__ rowsq = nullptr, float* __restrict__ rowsql = nullptr,
+                                   int rowsq_ld = 0) {
   const int b = blockIdx.x;
-  const float* src = x32 + (static_cast<size_t>(b) * S + S - 1) * H;
+  const size_t srow = static_cast<size_t>(b) * S + S - 1;
+  const float* src = x32 + srow * H;
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     const float v = src[c];
     xl32[static_cast<size_t>(b) * H + c] = v;
     xlb[static_cast<size_t>(b) * H + c] = __float2bfloat16(v);
   }
+  if (rowsq)
+    for (int p = threadIdx.x; p < rowsq_ld; p += blockDim.x)
+      rowsql[static_cast<size_t>(b) * rowsq_ld + p] = rowsq[srow * rowsq_ld + p];
 }
 
 // hf[b, :] = logit_scale * x[b] * rsqrt(mean(x[b]^2) + eps) * w   (f32; final norm of

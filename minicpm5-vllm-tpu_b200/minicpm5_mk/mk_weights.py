@@ -18,6 +18,9 @@ the parts this path keeps, re-laid-out for the tcgen05 GEMMs:
   weight-only int8 does not need that).
 * RoPE tables: inv_freq = theta^(-2i/hd) and angles in float64, cos/sin stored as f32
   [max_seq, hd/2] (`benchmark/f32_golden.py:45-50`; the [f, f] duplication is implicit).
+* RoPE is applied in the QKV GEMM epilogue.  To keep each rotation pair (i, i + hd/2) in adjacent
+  output columns, the Q and K rows of every head are reordered to (0, hd/2, 1, hd/2 + 1, ...).
+  Q and K use the same order, so Q.K (and the attention result) is unchanged; V keeps its order.
 """
 
 from __future__ import annotations
@@ -66,14 +69,27 @@ def deinterleave_gu(x: torch.Tensor, block: int = GU_BLOCK) -> Tuple[torch.Tenso
     return v[:, 0].reshape(n2 // 2, *x.shape[1:]), v[:, 1].reshape(n2 // 2, *x.shape[1:])
 
 
+def rope_pair_order(head_dim: int) -> torch.Tensor:
+    """Row order that makes rotation pairs adjacent: new row 2j <- j, new row 2j+1 <- j + hd/2."""
+    half = head_dim // 2
+    return torch.stack([torch.arange(half), torch.arange(half) + half], dim=1).reshape(-1)
+
+
+def pair_heads(w: torch.Tensor, n_heads: int, head_dim: int) -> torch.Tensor:
+    """Reorder the rows of every head of a [n_heads*head_dim, ...] projection into rope_pair_order."""
+    perm = rope_pair_order(head_dim).to(w.device)
+    return w.reshape(n_heads, head_dim, *w.shape[1:])[:, perm].reshape(w.shape)
+
+
 def prepare_layer(sd: Dict[str, torch.Tensor], cfg: MkConfig, i: int) -> Dict[str, torch.Tensor]:
     p = f"model.layers.{i}."
     f = lambda n: sd[p + n].to(F32)  # noqa: E731
     g_in = f("input_layernorm.weight")
     g_post = f("post_attention_layernorm.weight")
     sm = 1.0 / math.sqrt(cfg.head_dim)
-    wq = f("self_attn.q_proj.weight") * sm
-    wqkv = torch.cat([wq, f("self_attn.k_proj.weight"), f("self_attn.v_proj.weight")], 0) * g_in[None, :]
+    wq = pair_heads(f("self_attn.q_proj.weight") * sm, cfg.n_q, cfg.head_dim)
+    wk = pair_heads(f("self_attn.k_proj.weight"), cfg.n_kv, cfg.head_dim)
+    wqkv = torch.cat([wq, wk, f("self_attn.v_proj.weight")], 0) * g_in[None, :]
     w_qkv, s_qkv = quantize_per_out_channel(wqkv)
     w_o, s_o = quantize_per_out_channel(f("self_attn.o_proj.weight"))
     wg = f("mlp.gate_proj.weight") * g_post[None, :]

@@ -3,8 +3,9 @@
 The same forward as oracle/golden.py, but on the prepared int8 weight-only weights and with bf16
 rounding at exactly the points where the CUDA kernels round: the residual stream stays f32 and its
 bf16 copy feeds the projections; projection outputs (q/k/v, attention output, SiLU(g)*u) are stored
-in bf16; f32 accumulation; f32 scales applied in the GEMM epilogue; attention probabilities rounded
-to bf16 before P @ V in the prefill kernel.  It lets the GPU parity tests use tolerances near bf16
+in bf16; RoPE is applied in f32 to the un-rounded q/k (pair-interleaved head layout of the prepared
+weights) before that rounding; f32 accumulation; f32 scales applied in the GEMM epilogue; attention
+probabilities rounded to bf16 before P @ V in the prefill kernel.  It lets the GPU parity tests use tolerances near bf16
 resolution, separately from the accuracy of the design against the FP32 golden.
 
 It follows the same reference steps as oracle/golden.py (benchmark/f32_golden.py:78-102) and the
@@ -33,12 +34,16 @@ def _rstd(x: torch.Tensor, eps: float) -> torch.Tensor:
     return torch.rsqrt(torch.mean(x * x, dim=-1, keepdim=True) + eps)
 
 
-def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x: (rows, heads, hd) bf16-valued f32; cos/sin: (rows, hd/2)."""
-    h = x.shape[-1] // 2
-    a, b = x[..., :h], x[..., h:]
+def _rope_pairs(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """RoPE in the kernels' pair-interleaved head layout (columns 2j, 2j+1 = dims j, j + hd/2),
+    applied in f32 to the un-rounded projection and rounded to bf16 once.
+    x: (rows, heads, hd) f32; cos/sin: (rows, hd/2)."""
+    a, b = x[..., 0::2], x[..., 1::2]
     c, s = cos[:, None, :], sin[:, None, :]
-    return bf(torch.cat([a * c - b * s, b * c + a * s], dim=-1))
+    out = torch.empty_like(x)
+    out[..., 0::2] = a * c - b * s
+    out[..., 1::2] = b * c + a * s
+    return bf(out)
 
 
 def _deinterleave(t: torch.Tensor, block: int = 64):
@@ -86,10 +91,10 @@ def mirror_forward(ids: torch.Tensor, pw: dict, cfg):
         x = E[ids[b].long()] * cfg.scale_emb  # f32 residual stream
         for l in range(L - 1):
             Wqkv, sqkv = _deq(pw["w_qkv"][l]), pw["s_qkv"][l]
-            qkv = bf((bf(x) @ Wqkv.T) * _rstd(x, cfg.eps) * sqkv)
-            q = _rope(qkv[:, :qd].reshape(S, nq, hd), cos, sin)
-            k = _rope(qkv[:, qd:qd + kvd].reshape(S, nkv, hd), cos, sin)
-            v = qkv[:, qd + kvd:].reshape(S, nkv, hd)
+            qkv = (bf(x) @ Wqkv.T) * _rstd(x, cfg.eps) * sqkv
+            q = _rope_pairs(qkv[:, :qd].reshape(S, nq, hd), cos, sin)
+            k = _rope_pairs(qkv[:, qd:qd + kvd].reshape(S, nkv, hd), cos, sin)
+            v = bf(qkv[:, qd + kvd:]).reshape(S, nkv, hd)
             a = _attn_prefill(q, k, v, G)
             x = x + r * ((a @ _deq(pw["w_o"][l]).T) * pw["s_o"][l])
             gu = (bf(x) @ _deq(pw["w_gu"][l]).T) * _rstd(x, cfg.eps) * pw["s_gu"][l]
@@ -99,12 +104,12 @@ def mirror_forward(ids: torch.Tensor, pw: dict, cfg):
         l = L - 1
         Wqkv, sqkv = _deq(pw["w_qkv"][l]), pw["s_qkv"][l]
         rs = _rstd(x, cfg.eps)
-        kv = bf((bf(x) @ Wqkv[qd:].T) * rs * sqkv[qd:])
-        k = _rope(kv[:, :kvd].reshape(S, nkv, hd), cos, sin)
-        v = kv[:, kvd:].reshape(S, nkv, hd)
+        kv = (bf(x) @ Wqkv[qd:].T) * rs * sqkv[qd:]
+        k = _rope_pairs(kv[:, :kvd].reshape(S, nkv, hd), cos, sin)
+        v = bf(kv[:, kvd:]).reshape(S, nkv, hd)
         xl = x[-1:]
-        ql = bf((bf(xl) @ Wqkv[:qd].T) * _rstd(xl, cfg.eps) * sqkv[:qd])
-        ql = _rope(ql.reshape(1, nq, hd), cos[-1:], sin[-1:])[0]
+        ql = (bf(xl) @ Wqkv[:qd].T) * _rstd(xl, cfg.eps) * sqkv[:qd]
+        ql = _rope_pairs(ql.reshape(1, nq, hd), cos[-1:], sin[-1:])[0]
         kr = k.repeat_interleave(G, dim=1)
         vr = v.repeat_interleave(G, dim=1)
         s = torch.einsum("hd,khd->hk", ql, kr)
