@@ -69,8 +69,11 @@ mk_status device_state(DeviceState** out) {
     void* p = nullptr;
     MK_CUDA(cudaGetSymbolAddress(&p, g_mk_err));
     d.err = static_cast<int*>(p);
-    MK_CUDA(cudaFuncSetAttribute(mk::gemm_w8a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::G_SMEM_BYTES)));
+    for (auto fn : {mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE>, mk::gemm_w8a16_kernel<MK_GEMM_RESID>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU>, mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_RESID32>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(mk::G_SMEM_BYTES)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::AttnShape<96>::SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -160,7 +163,25 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.err = d->err;
   const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
-  mk::gemm_w8a16_kernel<<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+  switch (mode) {
+    case MK_GEMM_ROWSCALE:
+      mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+      break;
+    case MK_GEMM_RESID:
+      mk::gemm_w8a16_kernel<MK_GEMM_RESID><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+      break;
+    case MK_GEMM_SWIGLU:
+      mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+      break;
+    case MK_GEMM_COLSCALE:
+      mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+      break;
+    case MK_GEMM_RESID32:
+      mk::gemm_w8a16_kernel<MK_GEMM_RESID32><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
+      break;
+    default:
+      return MK_ERR_BAD_ARG;
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -371,13 +392,13 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
   w.qkv = take(T * h->n_qkv * 2);
   w.attn = take(T * h->q_dim * 2);
   w.hbuf = take(T * c.inter * 2);
-  w.rowsq = take(T * (c.hidden / 128) * 4);
+  w.rowsq = take(T * (c.hidden / 64) * 4);
   w.xl32 = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.xlb = take(static_cast<size_t>(bs) * c.hidden * 2);
   w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
-  w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 128) * 4);
+  w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 64) * 4);
   w.hf = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.logits = take(static_cast<size_t>(bs) * c.vocab * 4);
   w.pval = take(static_cast<size_t>(bs) * kLmParts * 4);
@@ -446,7 +467,7 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   MK_TRY(map_a(&mhl, hl, bs, I, I));
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
-  const int np = H / 128;       // 128-column tiles of the residual: RMSNorm partial sums per row
+  const int np = H / 64;        // 64-column segments of the residual: RMSNorm partial sums per row
   mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
       d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err, rowsq, np);
   MK_CUDA(cudaGetLastError());

@@ -25,9 +25,10 @@
 //   warp 0 lane 0 : TMA producer of the A tiles (256 x 64 bf16, 128B swizzle), 4-slot ring
 //   warp 0 lane 1 : TMA producer of the int8 weight tiles (128 x 64), 4-slot ring that runs ahead
 //   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (2 x M=128, N=128, K=16)
-//   warps 2..5    : epilogue (TMEM -> registers -> global), one 32-lane TMEM quarter each; while a
-//                   tile's main loop runs they prefetch that tile's residual rows into L2
-//   warps 6..13   : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
+//   warps 2..9    : epilogue (TMEM -> registers -> global): two warps per 32-lane TMEM quarter, each
+//                   owning 64 of the tile's 128 columns; while a tile's main loop runs they prefetch
+//                   that tile's residual rows into L2
+//   warps 10..13  : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
 // The three rings are decoupled so the weight loads and their conversion run ahead of the MMAs and
 // only the A-tile load latency has to be covered by the A ring.  TMEM holds two 128x256 f32
 // accumulators (2 x 256 columns, each two 128x128 halves) so the epilogue of tile i overlaps the main
@@ -48,8 +49,10 @@ constexpr int GA_SLOTS = 4;
 constexpr int GQ_SLOTS = 4;
 constexpr int GH_SLOTS = 3;
 constexpr int G_THREADS = 448;
-constexpr int G_CONV_WARP0 = 6;
-constexpr int G_CONV_WARPS = 8;
+constexpr int G_EPI_WARP0 = 2;
+constexpr int G_EPI_WARPS = 8;   // two per TMEM lane quarter, each owning half of the tile's columns
+constexpr int G_CONV_WARP0 = G_EPI_WARP0 + G_EPI_WARPS;
+constexpr int G_CONV_WARPS = 4;
 constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 32 KB (two 16 KB halves)
 constexpr uint32_t G_BQ_BYTES = GN * GK;        // 8 KB
 constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 16 KB
@@ -68,8 +71,8 @@ struct GemmArgs {
   float resid_scale;
   float* resid32;          // [M, ld_resid32] (RESID32)
   int ld_resid32;
-  // Fused RMSNorm statistics.  RESID32 writes, per row and 128-column tile, the sum of squares of
-  // the updated residual into rowsq[row * rowsq_ld + tile].  ROWSCALE / SWIGLU with rowsq != null
+  // Fused RMSNorm statistics.  RESID32 writes, per row and 64-column half tile, the sum of squares
+  // of the updated residual into rowsq[row * rowsq_ld + 2 * tile + half].  ROWSCALE / SWIGLU with rowsq != null
   // take rstd = rsqrt(sum over rowsq_np partials / norm_dim + eps) instead of row_scale.
   float* rowsq;
   int rowsq_ld, rowsq_np;
@@ -87,7 +90,8 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-__global__ void __launch_bounds__(G_THREADS, 1)
+template <int MODE>
+__global__ void __maxnreg__(144)
     gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
   extern __shared__ uint8_t g_smem_raw[];
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], G_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -220,22 +224,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
   } else if (warp < G_CONV_WARP0) {
     // -------------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int ch = (warp - G_EPI_WARP0) >> 2;     // which half of the tile's columns
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = blockIdx.x + it * gridDim.x;
       const int mb = tile / num_n, nb = tile % num_n;
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      if (args.mode == GEMM_RESID32) {
+      if (MODE == GEMM_RESID32) {
         // pull this tile's residual row segments (128 f32 = 512 B per row) into L2 while the main loop runs
 #pragma unroll
         for (int mi = 0; mi < GM / UM; ++mi) {
           const int row = mb * GM + mi * UM + q * 32 + lane;
           if (row < args.M) {
             const char* xr = reinterpret_cast<const char*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 +
-                                                           nb * GN);
+                                                           nb * GN + ch * (GN / 2));
 #pragma unroll
-            for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
+            for (int l2 = 0; l2 < 2; ++l2) prefetch_l2(xr + l2 * 128);
           }
         }
       }
@@ -247,7 +252,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const bool row_ok = row < args.M;
         const uint32_t tbase = tmem_base + a * 2 * GN + mi * GN + (static_cast<uint32_t>(q * 32) << 16);
         float rs = 1.0f;
-        if ((args.mode == GEMM_ROWSCALE || args.mode == GEMM_SWIGLU) && row_ok) {
+        if ((MODE == GEMM_ROWSCALE || MODE == GEMM_SWIGLU) && row_ok) {
           if (args.rowsq) {
             const float* ps = args.rowsq + static_cast<size_t>(row) * args.rowsq_ld;
             float ss = 0.f;
@@ -258,21 +263,21 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
         }
         float sumsq = 0.f;  // RESID32: sum of squares of this row's updated 128-column segment
-        if (args.mode == GEMM_SWIGLU) {
+        if (MODE == GEMM_SWIGLU) {
           const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
           const int i0 = nb * (GN / 2);     // output channels
 #pragma unroll 1
-          for (int c0 = 0; c0 < GN / 2; c0 += 32) {
-            uint32_t g[32], u[32];
-            tmem_ld_32x32b_x32(tbase + c0, g);
-            tmem_ld_32x32b_x32(tbase + GN / 2 + c0, u);
+          for (int c0 = ch * 32; c0 < ch * 32 + 32; c0 += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld_32x32b_x16(tbase + c0, g);
+            tmem_ld_32x32b_x16(tbase + GN / 2 + c0, u);
             tmem_ld_wait();
             if (row_ok) {
               const float4* sg = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
               const float4* su = reinterpret_cast<const float4*>(args.col_scale + n0 + GN / 2 + c0);
-              uint32_t o[16];
+              uint32_t o[8];
 #pragma unroll
-              for (int v = 0; v < 8; ++v) {
+              for (int v = 0; v < 4; ++v) {
                 const float4 a4 = __ldg(sg + v), b4 = __ldg(su + v);
                 const float ga[4] = {a4.x, a4.y, a4.z, a4.w}, ub[4] = {b4.x, b4.y, b4.z, b4.w};
                 float hv[4];
@@ -284,14 +289,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
               }
               uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0);
-#pragma unroll
-              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
             }
           }
         } else {
           const int n0 = nb * GN;
 #pragma unroll 1
-          for (int c0 = 0; c0 < GN; c0 += 32) {
+          for (int c0 = ch * (GN / 2); c0 < (ch + 1) * (GN / 2); c0 += 32) {
             uint32_t acc[32];
             tmem_ld_32x32b_x32(tbase + c0, acc);
             tmem_ld_wait();
@@ -308,7 +313,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               }
               uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
               uint32_t o[16];
-              if (args.mode == GEMM_RESID32) {
+              if (MODE == GEMM_RESID32) {
                 float4* xr =
                     reinterpret_cast<float4*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0);
                 const float r = args.resid_scale;
@@ -327,7 +332,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                   o[2 * v] = pack_bf16x2(x.x, x.y);
                   o[2 * v + 1] = pack_bf16x2(x.z, x.w);
                 }
-              } else if (args.mode == GEMM_RESID) {
+              } else if (MODE == GEMM_RESID) {
                 uint4 xin[4];
 #pragma unroll
                 for (int v = 0; v < 4; ++v) xin[v] = dst[v];
@@ -362,8 +367,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
             }
           }
-          if (args.mode == GEMM_RESID32 && args.rowsq && row_ok)
-            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + nb] = sumsq;
+          if (MODE == GEMM_RESID32 && args.rowsq && row_ok)
+            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + 2 * nb + ch] = sumsq;
         }
       }
       tc_fence_before();
