@@ -91,7 +91,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 }
 
 template <int MODE>
-__global__ void __maxnreg__(144)
+__global__ void __launch_bounds__(G_THREADS, 1)
     gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
   extern __shared__ uint8_t g_smem_raw[];
