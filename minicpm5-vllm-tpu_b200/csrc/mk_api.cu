@@ -392,13 +392,13 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
   w.qkv = take(T * h->n_qkv * 2);
   w.attn = take(T * h->q_dim * 2);
   w.hbuf = take(T * c.inter * 2);
-  w.rowsq = take(T * (c.hidden / 64) * 4);
+  w.rowsq = take(T * (c.hidden / 128) * 4);
   w.xl32 = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.xlb = take(static_cast<size_t>(bs) * c.hidden * 2);
   w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
-  w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 64) * 4);
+  w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 128) * 4);
   w.hf = take(static_cast<size_t>(bs) * c.hidden * 4);
   w.logits = take(static_cast<size_t>(bs) * c.vocab * 4);
   w.pval = take(static_cast<size_t>(bs) * kLmParts * 4);
@@ -467,7 +467,7 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
   MK_TRY(map_a(&mhl, hl, bs, I, I));
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
-  const int np = H / 64;        // 64-column segments of the residual: RMSNorm partial sums per row
+  const int np = H / 128;       // 128-column tiles of the residual: RMSNorm partial sums per row
   mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
       d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err, rowsq, np);
   MK_CUDA(cudaGetLastError());

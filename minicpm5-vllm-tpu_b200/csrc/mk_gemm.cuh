@@ -25,10 +25,9 @@
 //   warp 0 lane 0 : TMA producer of the A tiles (256 x 64 bf16, 128B swizzle), 4-slot ring
 //   warp 0 lane 1 : TMA producer of the int8 weight tiles (128 x 64), 4-slot ring that runs ahead
 //   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (2 x M=128, N=128, K=16)
-//   warps 2..9    : epilogue (TMEM -> registers -> global): two warps per 32-lane TMEM quarter, each
-//                   owning 64 of the tile's 128 columns; while a tile's main loop runs they prefetch
-//                   that tile's residual rows into L2
-//   warps 10..13  : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
+//   warps 2..5    : epilogue (TMEM -> registers -> global), one 32-lane TMEM quarter each; while a
+//                   tile's main loop runs they prefetch that tile's residual rows into L2
+//   warps 6..13   : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
 // The three rings are decoupled so the weight loads and their conversion run ahead of the MMAs and
 // only the A-tile load latency has to be covered by the A ring.  TMEM holds two 128x256 f32
 // accumulators (2 x 256 columns, each two 128x128 halves) so the epilogue of tile i overlaps the main
@@ -50,9 +49,9 @@ constexpr int GQ_SLOTS = 4;
 constexpr int GH_SLOTS = 3;
 constexpr int G_THREADS = 448;
 constexpr int G_EPI_WARP0 = 2;
-constexpr int G_EPI_WARPS = 8;   // two per TMEM lane quarter, each owning half of the tile's columns
+constexpr int G_EPI_WARPS = 4;   // one per 32-lane TMEM quarter
 constexpr int G_CONV_WARP0 = G_EPI_WARP0 + G_EPI_WARPS;
-constexpr int G_CONV_WARPS = 4;
+constexpr int G_CONV_WARPS = 8;
 constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 32 KB (two 16 KB halves)
 constexpr uint32_t G_BQ_BYTES = GN * GK;        // 8 KB
 constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 16 KB
@@ -71,8 +70,8 @@ struct GemmArgs {
   float resid_scale;
   float* resid32;          // [M, ld_resid32] (RESID32)
   int ld_resid32;
-  // Fused RMSNorm statistics.  RESID32 writes, per row and 64-column half tile, the sum of squares
-  // of the updated residual into rowsq[row * rowsq_ld + 2 * tile + half].  ROWSCALE / SWIGLU with rowsq != null
+  // Fused RMSNorm statistics.  RESID32 writes, per row and 128-column tile, the sum of squares of
+  // the updated residual into rowsq[row * rowsq_ld + tile].  ROWSCALE / SWIGLU with rowsq != null
   // take rstd = rsqrt(sum over rowsq_np partials / norm_dim + eps) instead of row_scale.
   float* rowsq;
   int rowsq_ld, rowsq_np;
@@ -225,7 +224,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   } else if (warp < G_CONV_WARP0) {
     // -------------------------------------------------------------------- epilogue
     const int q = warp & 3;                       // TMEM lane quarter this warp may access
-    const int ch = (warp - G_EPI_WARP0) >> 2;     // which half of the tile's columns
+    constexpr int ch = 0;                         // columns handled: the whole tile
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = blockIdx.x + it * gridDim.x;
       const int mb = tile / num_n, nb = tile % num_n;
@@ -238,9 +237,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const int row = mb * GM + mi * UM + q * 32 + lane;
           if (row < args.M) {
             const char* xr = reinterpret_cast<const char*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 +
-                                                           nb * GN + ch * (GN / 2));
+                                                           nb * GN);
 #pragma unroll
-            for (int l2 = 0; l2 < 2; ++l2) prefetch_l2(xr + l2 * 128);
+            for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
           }
         }
       }
@@ -267,7 +266,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
           const int i0 = nb * (GN / 2);     // output channels
 #pragma unroll 1
-          for (int c0 = ch * 32; c0 < ch * 32 + 32; c0 += 16) {
+          for (int c0 = 0; c0 < GN / 2; c0 += 16) {
             uint32_t g[16], u[16];
             tmem_ld_32x32b_x16(tbase + c0, g);
             tmem_ld_32x32b_x16(tbase + GN / 2 + c0, u);
@@ -296,7 +295,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         } else {
           const int n0 = nb * GN;
 #pragma unroll 1
-          for (int c0 = ch * (GN / 2); c0 < (ch + 1) * (GN / 2); c0 += 32) {
+          for (int c0 = 0; c0 < GN; c0 += 32) {
             uint32_t acc[32];
             tmem_ld_32x32b_x32(tbase + c0, acc);
             tmem_ld_wait();
@@ -368,7 +367,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
           }
           if (MODE == GEMM_RESID32 && args.rowsq && row_ok)
-            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + 2 * nb + ch] = sumsq;
+            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + nb] = sumsq;
         }
       }
       tc_fence_before();
