@@ -49,7 +49,7 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
-    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_down", "attn"],
+    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_kv", "gemm_down", "attn"],
                     help="time one isolated kernel of the forward (profiling driver) instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
     ap.add_argument("--kernel-iters", type=int, default=3)
@@ -70,7 +70,7 @@ def run_kernel(a):
     H, I = cfg.hidden, cfg.inter
     if a.kernel.startswith("gemm"):
         N, K, mode = {"gemm_swiglu": (2 * I, H, _lib.MK_GEMM_SWIGLU), "gemm_qkv": (cfg.qkv_dim, H, _lib.MK_GEMM_ROWSCALE),
-                      "gemm_o": (H, cfg.q_dim, _lib.MK_GEMM_RESID32),
+                      "gemm_o": (H, cfg.q_dim, _lib.MK_GEMM_RESID32), "gemm_kv": (2 * cfg.kv_dim, H, _lib.MK_GEMM_ROWSCALE),
                       "gemm_down": (H, I, _lib.MK_GEMM_RESID32)}[a.kernel]
         x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
         w8, s = quantize_per_out_channel(torch.randn((N, K), generator=g, device=dev) * 0.02)

@@ -348,9 +348,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 const int pos = args.rope_pos_base + row % args.rope_seq;
                 const float* ct = args.rope_cos + static_cast<size_t>(pos) * (args.head_dim >> 1);
                 const float* st = args.rope_sin + static_cast<size_t>(pos) * (args.head_dim >> 1);
+                // head-local column of this 32-column chunk; a chunk crosses at most one head boundary
+                const int hl0 = (n0 + c0) % args.head_dim;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                  const int pj = ((n0 + c0 + 2 * j) % args.head_dim) >> 1;
+                  int hl = hl0 + 2 * j;
+                  hl = hl >= args.head_dim ? hl - args.head_dim : hl;
+                  const int pj = hl >> 1;
                   const float c = __ldg(ct + pj), sn = __ldg(st + pj);
                   const float xa = __uint_as_float(acc[2 * j]) * rs * sc[2 * j];
                   const float xb = __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1];
