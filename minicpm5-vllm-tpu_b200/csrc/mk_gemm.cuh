@@ -243,6 +243,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
         }
       }
+      // per-row scalars that do not depend on the accumulator: fetched before waiting for it
+      float rs2[GM / UM];
+#pragma unroll
+      for (int mi = 0; mi < GM / UM; ++mi) {
+        const int row = mb * GM + mi * UM + q * 32 + lane;
+        rs2[mi] = 1.0f;
+        if ((MODE == GEMM_ROWSCALE || MODE == GEMM_SWIGLU) && row < args.M) {
+          if (args.rowsq) {
+            const float* ps = args.rowsq + static_cast<size_t>(row) * args.rowsq_ld;
+            float ss = 0.f;
+            for (int p = 0; p < args.rowsq_np; ++p) ss += ps[p];
+            rs2[mi] = rsqrtf(ss * args.inv_norm_dim + args.eps);
+          } else {
+            rs2[mi] = __ldg(args.row_scale + row);
+          }
+        }
+      }
       if (!mbar_wait(&tfull[a], aph, abort_flag)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -250,17 +267,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const int row = mb * GM + mi * UM + q * 32 + lane;
         const bool row_ok = row < args.M;
         const uint32_t tbase = tmem_base + a * 2 * GN + mi * GN + (static_cast<uint32_t>(q * 32) << 16);
-        float rs = 1.0f;
-        if ((MODE == GEMM_ROWSCALE || MODE == GEMM_SWIGLU) && row_ok) {
-          if (args.rowsq) {
-            const float* ps = args.rowsq + static_cast<size_t>(row) * args.rowsq_ld;
-            float ss = 0.f;
-            for (int p = 0; p < args.rowsq_np; ++p) ss += ps[p];
-            rs = rsqrtf(ss * args.inv_norm_dim + args.eps);
-          } else {
-            rs = __ldg(args.row_scale + row);
-          }
-        }
+        const float rs = mi == 0 ? rs2[0] : rs2[1];
         float sumsq = 0.f;  // RESID32: sum of squares of this row's updated 128-column segment
         if (MODE == GEMM_SWIGLU) {
           const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
