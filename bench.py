@@ -248,10 +248,12 @@ def main():
     from minicpm5_mk.mk_config import get_config
     from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
 
+    from minicpm5_mk.replicas import shard_bounds
+
     cfg = get_config(a.config).replace(max_seq=max(a.seq, 8192))
-    if a.global_bs % world:
-        raise SystemExit(f"global batch {a.global_bs} not divisible by {world} ranks")
-    bs = a.global_bs // world
+    _, bs = shard_bounds(a.global_bs, world, rank)  # this replica's block of sequences
+    if bs == 0:
+        raise SystemExit(f"global batch {a.global_bs} leaves rank {rank} without sequences")
     S = a.seq
     T = bs * S
 
@@ -333,7 +335,7 @@ def main():
         wall_ms = (time.perf_counter() - t0) * 1e3 / a.steps
         e2e_ms = max_over_ranks(max(wall_ms, e0.elapsed_time(e1) / a.steps))
         e2e = {"value": round(total_tokens / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(e2e_ms, 3),
-               "h2d_bytes_per_step": int(T * 4) * world, "d2h_bytes_per_step": int(bs * 4) * world,
+               "h2d_bytes_per_step": int(a.global_bs * S * 4), "d2h_bytes_per_step": int(a.global_bs * 4),
                "api": "minicpm5_mk.ops.MkEngine.forward -> mk_forward (C ABI)"}
 
     # ---------------------------------------------------------------- latency at 1 x 8192
