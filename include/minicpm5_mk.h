@@ -38,7 +38,8 @@ typedef enum mk_status {
   MK_ERR_BAD_ARG = 5,        /* null handle / pointer, bad enum value */
   MK_ERR_NOT_BOUND = 6,      /* mk_forward before mk_bind_weights */
   MK_ERR_BAD_TOKEN = 7,      /* a token id outside [0, vocab) was seen */
-  MK_ERR_WORKSPACE = 8       /* workspace smaller than mk_workspace_size */
+  MK_ERR_WORKSPACE = 8,      /* workspace smaller than mk_workspace_size */
+  MK_ERR_TOO_LARGE = 9       /* request exceeds a fixed capacity of the library (see the entry point) */
 } mk_status;
 
 /* Model configuration: plugin/minicpm5_mk/model.py:561-567 plus the MiniCPM muP scalars.
@@ -166,6 +167,25 @@ mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, 
 int32_t mk_lm_head_parts(void);
 mk_status mk_lm_head_argmax(const float* h, int32_t bs, int32_t H, const void* lm_head, int32_t V, float* logits,
                             float* part_val, int32_t* part_idx, int32_t* top1, void* stream);
+
+/* ---------------------------------------------------------------- allocation-free variant
+ * No counterpart in the reference.  Same computation and results as mk_lm_head_argmax, for callers
+ * that cannot allocate device memory at call time -- for example a serving engine that has already
+ * reserved almost all of the GPU for weights and its KV cache, or a host runtime calling through a
+ * thin FFI without access to the framework's caching allocator, where a cudaMalloc / cudaFree pair per
+ * call could fail or stall every stream on the device.  The caller passes only the inputs and the
+ * outputs; the per-block argmax partials live in a fixed array inside the library.
+ *   - At most MK_LM_HEAD_NOALLOC_MAX_ROWS rows per call; larger bs returns MK_ERR_TOO_LARGE.
+ *   - The array (about 148 KiB) exists on every GPU that loads the library, until process exit.
+ *   - The first call on a device looks up the array's device address (with that device current);
+ *     make that first call before any stream capture on the device.
+ *   - Nothing in the array needs to start at zero: every slot a call reads was written earlier in
+ *     the same call.  Calls share the array, so calls that overlap on the GPU (different streams, or
+ *     different host threads on one device) race; serialise them on one stream.
+ *   - Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define MK_LM_HEAD_NOALLOC_MAX_ROWS 64
+mk_status mk_lm_head_argmax_noalloc(const float* h, int32_t bs, int32_t H, const void* lm_head, int32_t V,
+                                    float* logits, int32_t* top1, void* stream);
 
 #ifdef __cplusplus
 }

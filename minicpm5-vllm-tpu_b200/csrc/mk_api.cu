@@ -308,6 +308,7 @@ const char* mk_status_string(mk_status s) {
     case MK_ERR_NOT_BOUND: return "weights not bound";
     case MK_ERR_BAD_TOKEN: return "token id out of range";
     case MK_ERR_WORKSPACE: return "workspace too small";
+    case MK_ERR_TOO_LARGE: return "request exceeds a fixed library capacity";
   }
   return "unknown status";
 }
@@ -657,4 +658,48 @@ mk_status mk_lm_head_argmax(const float* hvec, int32_t bs, int32_t H, const void
                         static_cast<cudaStream_t>(stream));
 }
 
+// ------------------------------------------------------------------------------ allocation-free lm_head
 }  // extern "C"
+
+namespace {
+// Scratch of mk_lm_head_argmax_noalloc: per-block argmax values then indices for up to
+// MK_LM_HEAD_NOALLOC_MAX_ROWS rows.  One copy per device that loads the library, kept until exit.
+constexpr int kNoAllocRows = MK_LM_HEAD_NOALLOC_MAX_ROWS;
+constexpr size_t kNoAllocValBytes = static_cast<size_t>(kNoAllocRows) * kLmParts * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocValBytes + static_cast<size_t>(kNoAllocRows) * kLmParts * sizeof(int32_t);
+static __device__ __align__(256) unsigned char g_lm_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_lm_noalloc_scratch per device (host code may only use the symbol through
+// cudaGetSymbolAddress: its name on the host is a stand-in, not a device pointer).
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+
+mk_status noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  MK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return MK_ERR_BAD_ARG;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_lm_noalloc_scratch);
+    if (e != cudaSuccess || !p) return MK_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MK_OK;
+}
+}  // namespace
+
+extern "C" mk_status mk_lm_head_argmax_noalloc(const float* hvec, int32_t bs, int32_t H, const void* lm_head,
+                                               int32_t V, float* logits, int32_t* top1, void* stream) {
+  if (!hvec || !lm_head || !logits || !top1) return MK_ERR_BAD_ARG;
+  if (bs > kNoAllocRows) return MK_ERR_TOO_LARGE;
+  if (bs <= 0 || H <= 0 || H % 8 || V <= 0) return MK_ERR_BAD_SHAPE;
+  if (!aligned16(lm_head)) return MK_ERR_BAD_ALIGN;
+  DeviceState* d = nullptr;
+  MK_TRY(device_state(&d));
+  unsigned char* scratch = nullptr;
+  MK_TRY(noalloc_scratch(&scratch));
+  float* pval = reinterpret_cast<float*>(scratch);
+  int* pidx = reinterpret_cast<int*>(scratch + kNoAllocValBytes);
+  return lm_head_launch(d, hvec, bs, H, lm_head, V, logits, pval, pidx, top1, static_cast<cudaStream_t>(stream));
+}
