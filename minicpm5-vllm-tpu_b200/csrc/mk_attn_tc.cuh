@@ -14,7 +14,9 @@
 //   warp 1      TMEM allocator + single-thread MMA issuer.  For 64-key tile j it issues
 //                 S_t(j+1) = Q_t K_{j+1}^T into the other S buffer of tile t  (M=128, N=64, K=hd)
 //                 O_t += P_t(j) V_j  once the softmax has written P_t(j)        (M=128, N=hd, K=64)
-//               so the tensor core computes the next scores while the softmax works on this tile.
+//               so the tensor core computes the next scores while the softmax works on this tile;
+//               it relies on the in-order execution of one thread's tcgen05.mma ops instead of
+//               waiting for O_t += P_t(j-1) V before reusing its S buffer.
 //   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: thread i owns row i of S_t
 //               (TMEM lane i), loads its 64 scores once, takes the max, writes P = exp2(S*c - m) as
 //               bf16 pairs over the same TMEM columns (P_t aliases S_t).  The running max is only
@@ -170,10 +172,10 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         if (j + 1 < ntiles) {
           const int j1 = j + 1;
           if (!mbar_wait(&k_full[j1 % TA_STAGES], (j1 / TA_STAGES) & 1, abort_flag)) break;
-          // S buffer (j+1)&1 still holds P_t(j-1): O_t += P_t(j-1) V must have finished
-          if (j1 >= 2 && (!mbar_wait(&pv_done[0], (j - 1) & 1, abort_flag) ||
-                          !mbar_wait(&pv_done[1], (j - 1) & 1, abort_flag)))
-            break;
+          // S buffer (j+1)&1 still holds P_t(j-1), read by O_t += P_t(j-1) V.  tcgen05.mma ops issued
+          // by this thread execute in issue order, so S_t(j+1) (issued after that P V) overwrites P_t(j-1)
+          // only after it has been read: no wait, the tensor pipe stays full.  The softmax finished
+          // reading S_t(j-1) before it signalled p_ready for tile j-1, which this thread consumed.
           tc_fence_after();
           issue_s(j1);
         }
