@@ -130,8 +130,9 @@ typedef enum mk_gemm_mode {
 } mk_gemm_mode;
 
 /* W8A16 GEMM: acc[m, n] = sum_k a[m, k] * w[n, k]; a bf16 [M, lda], w int8 [N, K].
- * N % 128 == 0, K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
- * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream.
+ * N % 128 == 0, K % 64 == 0, lda % 8 == 0, ldo % 16 == 0, out 32-byte aligned.
+ * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream; 32-byte
+ * aligned, ld_resid32 % 8 == 0.
  * Replaces `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` (mk_jax.py:233-269) and the
  * gate/up half of `fused_mlp` (mk_mlp.py:68-145). */
 mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,

@@ -98,6 +98,7 @@ mk_status device_state(DeviceState** out) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 // A operand: bf16 [rows, ld], box 64 (K) x 256 (rows), 128-byte swizzle.
 mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
@@ -584,9 +585,10 @@ mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const 
   if (!a || !w || !col_scale || !out) return MK_ERR_BAD_ARG;
   MK_TRY(check_gemm_shape(M, N, K, mode));
   if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
-  if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned16(resid32) || ld_resid32 % 4 || ld_resid32 < N))
+  // the epilogue writes out (and reads/writes resid32) with 32-byte vector accesses
+  if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned32(resid32) || ld_resid32 % 8 || ld_resid32 < N))
     return resid32 ? MK_ERR_BAD_ALIGN : MK_ERR_BAD_ARG;
-  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
+  if (!aligned16(a) || !aligned16(w) || !aligned32(out) || lda % 8 || ldo % 16 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
   CUtensorMap ma, mb;

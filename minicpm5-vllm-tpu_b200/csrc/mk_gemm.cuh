@@ -231,15 +231,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       if (MODE == GEMM_RESID32) {
-        // pull this tile's residual row segments (128 f32 = 512 B per row) into L2 while the main loop runs
+        // Pull the residual row segments (128 f32 = 512 B per row) of the NEXT tile into L2 while this
+        // one is drained, so their loads hit L2 even when the epilogue is the bottleneck (the first
+        // tile also prefetches its own rows).
+#pragma unroll 1
+        for (int pt = (it == 0 ? 0 : 1); pt <= 1; ++pt) {
+          if (it + pt >= my_tiles) break;
+          const int ptile = blockIdx.x + (it + pt) * gridDim.x;
+          const int pmb = ptile / num_n, pnb = ptile % num_n;
 #pragma unroll
-        for (int mi = 0; mi < GM / UM; ++mi) {
-          const int row = mb * GM + mi * UM + q * 32 + lane;
-          if (row < args.M) {
-            const char* xr = reinterpret_cast<const char*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 +
-                                                           nb * GN);
+          for (int mi = 0; mi < GM / UM; ++mi) {
+            const int row = pmb * GM + mi * UM + q * 32 + lane;
+            if (row < args.M) {
+              const char* xr = reinterpret_cast<const char*>(args.resid32 +
+                                                             static_cast<size_t>(row) * args.ld_resid32 + pnb * GN);
 #pragma unroll
-            for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
+              for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
+            }
           }
         }
       }
@@ -294,9 +302,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 o[2 * v] = pack_bf16x2(hv[0], hv[1]);
                 o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
               }
-              uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0);
-              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+              st_global_v8(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0, o[0], o[1], o[2], o[3], o[4],
+                           o[5], o[6], o[7]);
             }
           }
         } else {
@@ -320,23 +327,24 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
               uint32_t o[16];
               if (MODE == GEMM_RESID32) {
-                float4* xr =
-                    reinterpret_cast<float4*>(args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0);
+                float* xr = args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0;
                 const float r = args.resid_scale;
-                float4 xv[8];
+                float xv[4][8];
 #pragma unroll
-                for (int v = 0; v < 8; ++v) xv[v] = xr[v];
+                for (int v = 0; v < 4; ++v) ld_global_v8(xr + 8 * v, xv[v]);
 #pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                  float4 x = xv[v];
-                  x.x += r * (__uint_as_float(acc[4 * v + 0]) * sc[4 * v + 0]);
-                  x.y += r * (__uint_as_float(acc[4 * v + 1]) * sc[4 * v + 1]);
-                  x.z += r * (__uint_as_float(acc[4 * v + 2]) * sc[4 * v + 2]);
-                  x.w += r * (__uint_as_float(acc[4 * v + 3]) * sc[4 * v + 3]);
-                  xr[v] = x;
-                  sumsq += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-                  o[2 * v] = pack_bf16x2(x.x, x.y);
-                  o[2 * v + 1] = pack_bf16x2(x.z, x.w);
+                for (int v = 0; v < 4; ++v) {
+                  float x[8];
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) {
+                    x[e] = xv[v][e] + r * (__uint_as_float(acc[8 * v + e]) * sc[8 * v + e]);
+                    sumsq += x[e] * x[e];
+                  }
+                  st_global_v8(xr + 8 * v, __float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]),
+                               __float_as_uint(x[3]), __float_as_uint(x[4]), __float_as_uint(x[5]),
+                               __float_as_uint(x[6]), __float_as_uint(x[7]));
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) o[4 * v + e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
                 }
               } else if (MODE == GEMM_RESID) {
                 uint4 xin[4];
@@ -373,8 +381,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                   o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * sc[2 * j],
                                      __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1]);
               }
-#pragma unroll
-              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              st_global_v8(dst, o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7]);
+              st_global_v8(dst + 2, o[8], o[9], o[10], o[11], o[12], o[13], o[14], o[15]);
             }
           }
           if (MODE == GEMM_RESID32 && args.rowsq && row_ok)
