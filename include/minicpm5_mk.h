@@ -55,7 +55,7 @@ typedef struct mk_config {
  *   rope_cos/sin   : f32  [max_seq, head_dim/2]
  *   w_qkv  int8 [L, (n_q+2 n_kv) head_dim, hidden]   s_qkv  f32 [L, (n_q+2 n_kv) head_dim]
  *   w_o    int8 [L, hidden, n_q head_dim]            s_o    f32 [L, hidden]
- *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows interleaved in blocks of 64)
+ *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows alternating: row 2i gate i, row 2i+1 up i)
  *                                                    s_gu   f32 [L, 2 inter]
  *   w_down int8 [L, hidden, inter]                   s_down f32 [L, hidden]
  * The Q rows carry 1/sqrt(head_dim); RMSNorm gains are folded into the weight columns. */
@@ -124,15 +124,14 @@ void mk_destroy(mk_handle* h);
 typedef enum mk_gemm_mode {
   MK_GEMM_ROWSCALE = 0, /* out = bf16(acc * row_scale[m] * col_scale[n])                     */
   MK_GEMM_RESID = 1,    /* out = bf16(out + resid_scale * acc * col_scale[n])   (in place)   */
-  MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g) * u) over 64-row gate/up blocks; out width N/2 */
+  MK_GEMM_SWIGLU = 2,   /* out[m, i] = bf16(silu(g_i) * u_i), rows 2i / 2i+1 = gate / up; out width N/2 */
   MK_GEMM_COLSCALE = 3, /* out = bf16(acc * col_scale[n])                                    */
   MK_GEMM_RESID32 = 4   /* resid32 += resid_scale * acc * col_scale[n] (f32, in place); out = bf16(resid32) */
 } mk_gemm_mode;
 
 /* W8A16 GEMM: acc[m, n] = sum_k a[m, k] * w[n, k]; a bf16 [M, lda], w int8 [N, K].
- * N % 128 == 0, K % 64 == 0, lda % 8 == 0, ldo % 16 == 0, out 32-byte aligned.
- * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream; 32-byte
- * aligned, ld_resid32 % 8 == 0.
+ * N % 128 == 0, K % 64 == 0, lda % 8 == 0, ldo % 8 == 0.
+ * resid32 (f32 [M, ld_resid32], RESID32 mode only, else NULL) is the f32 residual stream.
  * Replaces `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` (mk_jax.py:233-269) and the
  * gate/up half of `fused_mlp` (mk_mlp.py:68-145). */
 mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,

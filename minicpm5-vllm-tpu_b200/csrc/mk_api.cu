@@ -27,7 +27,7 @@ __device__ int g_mk_err;
 
 constexpr int kMaxDevices = 64;
 // Weight-operand TMA box rows (one int8 weight tile per k-step).
-constexpr int kWeightBoxRows = mk::GN;
+constexpr int kWeightBoxRows = mk::GW;
 constexpr int kLmParts = 296;
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -98,13 +98,12 @@ mk_status device_state(DeviceState** out) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
-// A operand: bf16 [rows, ld], box 64 (K) x 256 (rows), 128-byte swizzle.
+// Token operand: bf16 [rows, ld], box 64 (K) x gemm_nt(rows) (tokens), 128-byte swizzle.
 mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(mk::GM)};  // 64 x 256
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GKB), static_cast<cuuint32_t>(mk::gemm_nt(rows))};
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -112,21 +111,22 @@ mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
-// B operand: int8 [N, K] (K contiguous), box 64 (K) x box_rows (N), no swizzle.
-mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K, int box_rows = mk::GN) {
+// Weight operand: int8 [N, K] (K contiguous), box 128 (K) x box_rows (N), 128-byte swizzle (the
+// converters read one row per thread; the swizzle spreads a quarter-warp's rows over all banks).
+mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K, int box_rows = mk::GW) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
 // Optional fused epilogue work of one GEMM launch (RMSNorm statistics, RoPE).
 struct GemmFusion {
-  float* rowsq = nullptr;  // per-(row, 128-column tile) sums of squares of the f32 residual
+  float* rowsq = nullptr;  // per-(token, 128-channel tile) sums of squares of the f32 residual
   int rowsq_ld = 0, rowsq_np = 0;
   float inv_norm_dim = 0.f, eps = 0.f;
   const float* rope_cos = nullptr;
@@ -142,6 +142,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.M = M;
   ga.N = N;
   ga.K = K;
+  ga.nt = mk::gemm_nt(M);
   ga.mode = mode;
   ga.row_scale = row_scale;
   ga.col_scale = col_scale;
@@ -162,7 +163,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.rope_seq = fu.rope_seq > 0 ? fu.rope_seq : 1;
   ga.rope_pos_base = fu.rope_pos_base;
   ga.err = d->err;
-  const int tiles = ((M + mk::GM - 1) / mk::GM) * ((N + mk::GN - 1) / mk::GN);
+  const int tiles = ((M + ga.nt - 1) / ga.nt) * (N / mk::GW);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
   switch (mode) {
     case MK_GEMM_ROWSCALE:
@@ -188,8 +189,8 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
 
 mk_status check_gemm_shape(int M, int N, int K, int mode) {
   if (M <= 0 || N <= 0 || K <= 0) return MK_ERR_BAD_SHAPE;
-  if (N % 128 || K % mk::GK) return MK_ERR_BAD_SHAPE;
-  if (mode == MK_GEMM_SWIGLU && N % mk::GN) return MK_ERR_BAD_SHAPE;  // 64 gate + 64 up per tile
+  if (N % 128 || K % mk::GKB) return MK_ERR_BAD_SHAPE;
+  if (mode == MK_GEMM_SWIGLU && N % 2) return MK_ERR_BAD_SHAPE;  // alternating gate / up rows
   if (mode < 0 || mode > 4) return MK_ERR_BAD_ARG;
   return MK_OK;
 }
@@ -585,10 +586,9 @@ mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const 
   if (!a || !w || !col_scale || !out) return MK_ERR_BAD_ARG;
   MK_TRY(check_gemm_shape(M, N, K, mode));
   if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
-  // the epilogue writes out (and reads/writes resid32) with 32-byte vector accesses
-  if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned32(resid32) || ld_resid32 % 8 || ld_resid32 < N))
+  if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned16(resid32) || ld_resid32 % 4 || ld_resid32 < N))
     return resid32 ? MK_ERR_BAD_ALIGN : MK_ERR_BAD_ARG;
-  if (!aligned16(a) || !aligned16(w) || !aligned32(out) || lda % 8 || ldo % 16 || lda < K) return MK_ERR_BAD_ALIGN;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
   CUtensorMap ma, mb;

@@ -22,7 +22,6 @@ enum : int {
   DEV_ERR_TIMEOUT_ATTN = 0x200,
   DEV_ERR_BAD_TOKEN_ID = 0x300,
   DEV_ERR_TIMEOUT_ATTN_TC = 0x400,
-  DEV_ERR_TIMEOUT_GEMM_PAIR = 0x500,
 };
 
 // Wall-clock limit of one mbarrier wait.  Legitimate waits are microseconds long.
@@ -56,30 +55,41 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// A waiting thread is suspended until the phase completes (or this long), instead of re-polling and
+// taking issue slots from the warps that do the work.
+constexpr uint32_t kSuspendHintNs = 10000000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
 // Wait until the phase with the given parity has completed.  Returns false when the CTA-wide
 // abort flag is (or becomes) set, or when the wait exceeds kWaitLimitNs (then it sets the flag).
+// The clock and the flag are read only every kWaitPoll unsuccessful tries: reading %globaltimer
+// costs a few hundred nanoseconds, which would otherwise be added to every hand-off that finds
+// its barrier not yet complete.
+constexpr uint32_t kWaitPoll = 16;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  uint64_t t0 = 0;
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      return false;
+    if (n % kWaitPoll == 0) {
+      if (*abort_flag) return false;
+      const uint64_t t = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
@@ -87,56 +97,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait that ignores the abort flag (used while draining on the way out).
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(a, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-  }
-  return true;
-}
-
-// ---------------------------------------------------------------------------------- clusters
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory object in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-// Arrive on an mbarrier anywhere in the cluster (release at cluster scope).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (acquire at cluster scope) for barriers that CTAs of the cluster arrive on.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait_cluster(a, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      return false;
+  uint64_t t0 = 0;
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (n % kWaitPoll == 0) {
+      const uint64_t t = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > kWaitLimitNs) {
+        return false;
+      }
     }
   }
 }
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+
+// One lane of the (fully active) warp returns true.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ---------------------------------------------------------------------------------- TMA
@@ -180,42 +163,6 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// CTA-pair variants: the allocation, MMA and commit span both CTAs of a 2-CTA cluster.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D (M/2 rows in each CTA's TMEM) (+)= A (M/2 rows in each CTA's smem) * B^T (N/2 rows in each CTA's smem).
-__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the barrier at this shared-memory offset in every CTA of `cta_mask` when the pair's
-// prior tcgen05 ops have completed.
-__device__ __forceinline__ void mma_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
 // D(tmem) (+)= A(smem desc) * B(smem desc)^T, kind::f16 (bf16 inputs, f32 accumulate).
 __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -245,16 +192,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-// 32 lanes x 16 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
 }
@@ -373,21 +310,6 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_
       "}"
       : "=r"(lo), "=r"(hi)
       : "r"(w), "l"(0xCB000080CB000080ull));  // (-(2^23 + 128), -(2^23 + 128)) as f32 pairs
-}
-
-// 256-bit global accesses (sm_100): one instruction covers a full 32-byte sector.  Addresses must be
-// 32-byte aligned.
-__device__ __forceinline__ void st_global_v8(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t a4, uint32_t a5, uint32_t a6, uint32_t a7) {
-  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2),
-               "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
-               : "memory");
-}
-__device__ __forceinline__ void ld_global_v8(const void* p, float (&v)[8]) {
-  asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
-               : "l"(p)
-               : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {

@@ -1,37 +1,46 @@
-// W8A16 GEMM for sm_100a: tcgen05.mma (bf16 x bf16 -> f32 in TMEM) fed by TMA, with the int8
-// weight-only operand dequantised to bf16 in shared memory.
+// W8A16 GEMM for sm_100a: tcgen05.mma with the int8 weight-only operand dequantised straight into
+// tensor memory (the TMEM-A form of kind::f16), activations fed by TMA.
 //
-//   out[m, n] = epilogue( sum_k A[m, k] * Wq[n, k] )        A bf16 [M, K] row-major
+//   out[m, n] = epilogue( sum_k X[m, k] * Wq[n, k] )        X bf16 [M, K] row-major (tokens)
 //                                                           Wq int8 [N, K] row-major (per-output-
 //                                                           channel scale s[n], f32)
-// Epilogue modes (the per-row / per-column scalings commute with the sum, so they are applied to
-// the f32 accumulator read back from TMEM):
+// The UMMA computes the transposed tile D[n, m] = Wq_tile . X_tile^T: the weight tile (128 output
+// channels) is the A operand and lives in TMEM, the token tile is the B operand in shared memory.
+// So the converted weights never touch shared memory: per k-step the tensor core reads only the
+// token tile from shared memory, and the int8 -> bf16 conversion writes TMEM, which has its own
+// bandwidth.  (The first version kept the converted weights in shared memory as the B operand;
+// its shared-memory traffic per FLOP -- the tensor core reading both operands, TMA writes, the
+// converters' loads and stores -- capped it near half of the bf16 peak.)
+//
+// Epilogue modes (the per-token / per-channel scalings commute with the sum, so they are applied
+// to the f32 accumulator read back from TMEM):
 //   ROWSCALE : out = bf16(acc * rstd[m] * s[n])                   RMSNorm-fused projections (QKV),
 //              optionally with RoPE applied to the Q/K columns before the bf16 rounding
 //   RESID    : out = bf16(out + r * acc * s[n])   (in place)       bf16 residual
 //   RESID32  : x32 = x32 + r * acc * s[n] (f32, in place), out = bf16(x32)
 //              o_proj / down + scaled residual on the f32 residual stream; `out` is the bf16 copy
 //              the next projection reads as its A operand
-//   SWIGLU   : tile = 64 gate + 64 up channels (interleaved weight rows);
+//   SWIGLU   : weight rows alternate gate / up (row 2i = gate channel i, row 2i+1 = up channel i);
 //              h[m, i] = bf16(silu(g * rstd[m] * s_g) * (u * rstd[m] * s_u))   (out width N/2)
+//   COLSCALE : out = bf16(acc * s[n])
 //
 // Reference counterparts: `fused_qkv` (plugin/minicpm5_mk/mk_mlp.py:161-206), `linear` +
 // residual (plugin/minicpm5_mk/mk_jax.py:233-269, :394), `fused_mlp`
 // (plugin/minicpm5_mk/mk_mlp.py:68-145).
 //
-// CTA layout (persistent, one CTA per SM, 14 warps):
-// Tile = 256 rows of A x 128 output channels: two M=128 UMMAs share one converted weight tile,
-// so every converted weight element feeds 256 rows.
-//   warp 0 lane 0 : TMA producer of the A tiles (256 x 64 bf16, 128B swizzle), 4-slot ring
-//   warp 0 lane 1 : TMA producer of the int8 weight tiles (128 x 64), 4-slot ring that runs ahead
-//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (2 x M=128, N=128, K=16)
-//   warps 2..5    : epilogue (TMEM -> registers -> global), one 32-lane TMEM quarter each; while a
-//                   tile's main loop runs they prefetch that tile's residual rows into L2
-//   warps 6..13   : int8 -> bf16 converters filling a 3-slot ring of 128B-swizzled K-major B tiles
-// The three rings are decoupled so the weight loads and their conversion run ahead of the MMAs and
-// only the A-tile load latency has to be covered by the A ring.  TMEM holds two 128x256 f32
-// accumulators (2 x 256 columns, each two 128x128 halves) so the epilogue of tile i overlaps the main
-// loop of tile i+1.
+// CTA layout (persistent, one CTA per SM, 15 warps).  Tile = 128 output channels x nt tokens
+// (nt = 192, or the token count rounded up to 16 when M is smaller):
+//   warp 0 lane 0 : TMA producer of the token tiles (nt x 64 bf16, 128B swizzle), 6-slot ring
+//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=nt, K=16, A in TMEM)
+//   warp 2 lane 0 : TMA producer of the int8 weight tiles (128 x 64, 64B swizzle), 6-slot ring
+//   warps 3..10   : epilogue (TMEM -> registers -> global), two warps per 32-lane TMEM quarter
+//                   (= 32 output channels) taking alternate 32-token chunks; thread = channel,
+//                   registers = consecutive tokens, so every global access of a warp covers 32
+//                   consecutive channels of one token row
+//   warps 11..14  : int8 -> bf16 converters: shared memory -> registers -> tcgen05.st into a
+//                   4-slot TMEM weight ring (one warp per TMEM lane quarter)
+// TMEM (512 columns): two f32 accumulators of 192 columns (the epilogue of tile i overlaps the main
+// loop of tile i+1) + 4 weight slots of 32 columns (128 x 64 bf16, two K values per column).
 #pragma once
 
 #include "mk_common.cuh"
@@ -40,28 +49,40 @@ namespace mk {
 
 enum GemmMode : int { GEMM_ROWSCALE = 0, GEMM_RESID = 1, GEMM_SWIGLU = 2, GEMM_COLSCALE = 3, GEMM_RESID32 = 4 };
 
-constexpr int GM = 256;   // rows of A per tile: two UMMA M=128 halves sharing one converted weight tile
-constexpr int UM = 128;   // UMMA M
-constexpr int GN = 128;   // output channels per tile (UMMA N)
-constexpr int GK = 64;    // K per stage (one 128-byte swizzle row of bf16)
-constexpr int GA_SLOTS = 4;
-constexpr int GQ_SLOTS = 4;
-constexpr int GH_SLOTS = 3;
-constexpr int G_THREADS = 448;
-constexpr int G_EPI_WARP0 = 2;
-constexpr int G_EPI_WARPS = 4;   // one per 32-lane TMEM quarter
+constexpr int GW = 128;   // output channels per tile (UMMA M, TMEM lanes)
+constexpr int GT = 192;   // tokens per tile (UMMA N), upper bound of the runtime nt
+constexpr int GK = 128;   // K per pipeline stage
+constexpr int GKB = 64;   // K per token-tile TMA box (one 128-byte swizzle row of bf16)
+constexpr int GX_SLOTS = 3;
+constexpr int GQ_SLOTS = 3;
+constexpr int GW_SLOTS = 2;
+constexpr int G_THREADS = 608;
+constexpr int G_QPROD_WARP = 2;  // int8 weight-tile producer (its own warp: a waiting lane of a shared
+                                 // warp would hold up the other producer)
+constexpr int G_EPI_WARP0 = 3;
+constexpr int G_EPI_WARPS = 8;   // two per 32-lane TMEM quarter (alternate 32-token chunks)
 constexpr int G_CONV_WARP0 = G_EPI_WARP0 + G_EPI_WARPS;
-constexpr int G_CONV_WARPS = 8;
-constexpr uint32_t G_A_BYTES = GM * GK * 2;     // 32 KB (two 16 KB halves)
-constexpr uint32_t G_BQ_BYTES = GN * GK;        // 8 KB
-constexpr uint32_t G_BH_BYTES = GN * GK * 2;    // 16 KB
-constexpr uint32_t G_RING_BYTES = GA_SLOTS * G_A_BYTES + GQ_SLOTS * G_BQ_BYTES + GH_SLOTS * G_BH_BYTES;
+constexpr int G_CONV_WARPS = 8;  // two per 32-lane TMEM quarter (halves of the k-step)
+constexpr uint32_t G_XSUB_BYTES = GT * GKB * 2;  // 24 KB: one 64-wide K panel of a token tile
+constexpr uint32_t G_X_BYTES = 2 * G_XSUB_BYTES;  // 48 KB
+constexpr uint32_t G_Q_BYTES = GW * GK;          // 16 KB
 constexpr uint32_t G_TMEM_COLS = 512;
-constexpr size_t G_SMEM_BYTES = 1024 /*align pad*/ + G_RING_BYTES + 512 /*barriers*/;
+constexpr uint32_t G_W_COL0 = 2 * GT;         // weight ring after the two accumulators
+constexpr uint32_t G_W_COLS = GK / 2;         // 64 columns per weight slot
+static_assert(G_W_COL0 + GW_SLOTS * G_W_COLS <= G_TMEM_COLS, "TMEM budget");
+static_assert(G_XSUB_BYTES % 1024 == 0 && G_Q_BYTES % 1024 == 0, "swizzle atoms stay aligned");
+constexpr uint32_t G_RING_BYTES = GX_SLOTS * G_X_BYTES + GQ_SLOTS * G_Q_BYTES;
+constexpr uint32_t G_RS_FLOATS = 2 * GT;                 // per-token rstd, double-buffered
+constexpr uint32_t G_SS_FLOATS = 2 * 4 * GT;             // per-(lane quarter, token) sums of squares
+constexpr size_t G_SMEM_BYTES = 1024 /*align pad*/ + G_RING_BYTES + 4 * (G_RS_FLOATS + G_SS_FLOATS) + 512;
 static_assert(G_SMEM_BYTES <= 232448, "shared memory budget");
+
+// Tokens per tile for M tokens (a multiple of 16, the UMMA N granularity at M = 128).
+__host__ __device__ constexpr int gemm_nt(int M) { return M >= GT ? GT : ((M + 15) / 16) * 16; }
 
 struct GemmArgs {
   int M, N, K;
+  int nt;                  // tokens per tile (gemm_nt(M)); the token tensor map's box height
   int mode;
   const float* row_scale;  // [M] (ROWSCALE, SWIGLU)
   const float* col_scale;  // [N]
@@ -70,14 +91,14 @@ struct GemmArgs {
   float resid_scale;
   float* resid32;          // [M, ld_resid32] (RESID32)
   int ld_resid32;
-  // Fused RMSNorm statistics.  RESID32 writes, per row and 128-column tile, the sum of squares of
-  // the updated residual into rowsq[row * rowsq_ld + tile].  ROWSCALE / SWIGLU with rowsq != null
+  // Fused RMSNorm statistics.  RESID32 writes, per token and 128-channel tile, the sum of squares
+  // of the updated residual into rowsq[m * rowsq_ld + tile].  ROWSCALE / SWIGLU with rowsq != null
   // take rstd = rsqrt(sum over rowsq_np partials / norm_dim + eps) instead of row_scale.
   float* rowsq;
   int rowsq_ld, rowsq_np;
   float inv_norm_dim, eps;
   // Fused RoPE (ROWSCALE): columns [0, rope_cols) hold heads of width head_dim whose rotation pairs
-  // (i, i + head_dim/2) are stored interleaved as adjacent columns (2j, 2j + 1); position of row m
+  // (i, i + head_dim/2) are stored interleaved as adjacent columns (2j, 2j + 1); position of token m
   // is rope_pos_base + m % rope_seq; tables f32 [max_seq, head_dim/2].
   const float* rope_cos;
   const float* rope_sin;
@@ -89,26 +110,49 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+__device__ __forceinline__ void st_global_b16(__nv_bfloat16* p, float v) {
+  const __nv_bfloat16 b = __float2bfloat16_rn(v);
+  *p = b;
+}
+
+// v[j] (j = token of the chunk) summed over the 32 lanes; lane l returns the sum for token l.
+// Butterfly transpose-reduction: 31 shuffles for 32 sums, in a fixed order.
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = up ? v[i] : v[i + off];
+      const float keep = up ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(G_THREADS, 1)
-    gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                       const GemmArgs args) {
   extern __shared__ uint8_t g_smem_raw[];
   const uint32_t raw = smem_u32(g_smem_raw);
   uint8_t* sbase = g_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sA = sbase;                                   // [GA_SLOTS] 32 KB
-  uint8_t* sH = sA + GA_SLOTS * G_A_BYTES;               // [GH_SLOTS] 16 KB (bf16 B)
-  uint8_t* sQ = sH + GH_SLOTS * G_BH_BYTES;              // [GQ_SLOTS] 8 KB (int8 B)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + GQ_SLOTS * G_BQ_BYTES);
-  uint64_t* a_full = bars;                   // [GA_SLOTS] TMA landed
-  uint64_t* a_empty = a_full + GA_SLOTS;     // [GA_SLOTS] MMAs reading the slot finished
-  uint64_t* q_full = a_empty + GA_SLOTS;     // [GQ_SLOTS] TMA landed
+  uint8_t* sX = sbase;                                     // [GX_SLOTS] token tiles
+  uint8_t* sQ = sX + GX_SLOTS * G_X_BYTES;                 // [GQ_SLOTS] int8 weight tiles
+  float* rs_s = reinterpret_cast<float*>(sQ + GQ_SLOTS * G_Q_BYTES);  // [2][GT]
+  float* ss_s = rs_s + G_RS_FLOATS;                                    // [2][4][GT]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ss_s + G_SS_FLOATS);
+  uint64_t* x_full = bars;                   // [GX_SLOTS] TMA landed
+  uint64_t* x_empty = x_full + GX_SLOTS;     // [GX_SLOTS] MMAs reading the slot finished
+  uint64_t* q_full = x_empty + GX_SLOTS;     // [GQ_SLOTS] TMA landed
   uint64_t* q_empty = q_full + GQ_SLOTS;     // [GQ_SLOTS] converters read the slot
-  uint64_t* h_full = q_empty + GQ_SLOTS;     // [GH_SLOTS] converters wrote the slot
-  uint64_t* h_empty = h_full + GH_SLOTS;     // [GH_SLOTS] MMAs reading the slot finished
-  uint64_t* tfull = h_empty + GH_SLOTS;      // [2] accumulator ready
+  uint64_t* w_full = q_empty + GQ_SLOTS;     // [GW_SLOTS] converters wrote the TMEM weight slot
+  uint64_t* w_empty = w_full + GW_SLOTS;     // [GW_SLOTS] MMAs reading the TMEM slot finished
+  uint64_t* tfull = w_empty + GW_SLOTS;      // [2] accumulator ready
   uint64_t* tempty = tfull + 2;              // [2] accumulator drained by the epilogue
-  uint64_t* drain = tempty + 2;              // all MMAs finished
+  uint64_t* esync = tempty + 2;              // [2] epilogue warps' shared per-token values ready
+  uint64_t* drain = esync + 2;               // all MMAs finished
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -116,27 +160,28 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GA_SLOTS; ++s) {
-      mbar_init(&a_full[s], 1);
-      mbar_init(&a_empty[s], 1);
+    for (int s = 0; s < GX_SLOTS; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
     }
     for (int s = 0; s < GQ_SLOTS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], G_CONV_WARPS);
     }
-    for (int s = 0; s < GH_SLOTS; ++s) {
-      mbar_init(&h_full[s], G_CONV_WARPS);
-      mbar_init(&h_empty[s], 1);
+    for (int s = 0; s < GW_SLOTS; ++s) {
+      mbar_init(&w_full[s], G_CONV_WARPS);
+      mbar_init(&w_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], G_EPI_WARPS);
+      mbar_init(&esync[a], G_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, G_TMEM_COLS);
@@ -147,287 +192,305 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_m = (args.M + GM - 1) / GM;
-  const int num_n = (args.N + GN - 1) / GN;
-  const int num_tiles = num_m * num_n;
-  const int KT = args.K / GK;
+  const int nt = args.nt;
+  const int num_c = args.N / GW;                 // channel tiles
+  const int num_t = (args.M + nt - 1) / nt;      // token tiles
+  const int num_tiles = num_t * num_c;
+  const int KT = (args.K + GK - 1) / GK;  // K % 64 == 0; a last half stage covers K % 128 == 64
   const int my_tiles = (num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                        static_cast<int>(gridDim.x);
   const int total = my_tiles * KT;  // k-steps this CTA runs (slot index = k-step mod ring size)
 
-  if (warp == 0) {
-    if (lane < 2) {
-      // ------------------------------------------------------------------ TMA producers
-      // lane 0: A tiles into the A ring; lane 1: int8 weight tiles into the int8 ring.
-      const bool is_a = lane == 0;
-      const int slots = is_a ? GA_SLOTS : GQ_SLOTS;
-      uint64_t* full = is_a ? a_full : q_full;
-      uint64_t* empty = is_a ? a_empty : q_empty;
-      uint32_t issued = 0, issued_par = 0;
-      for (int idx = 0; idx < total; ++idx) {
-        const int s = idx % slots;
-        const uint32_t ph = (idx / slots) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-        const int tile = blockIdx.x + (idx / KT) * gridDim.x;
-        const int kt = idx % KT;
-        if (is_a) {
-          mbar_arrive_expect_tx(&full[s], G_A_BYTES);
-          tma_load_2d(sA + s * G_A_BYTES, &tmA, &full[s], kt * GK, (tile / num_n) * GM);
+  if (warp == 0 || warp == G_QPROD_WARP) {
+    // ------------------------------------------------------------------ TMA producers
+    // warp 0: token tiles into the X ring; warp 2: int8 weight tiles into the int8 ring.  The whole
+    // warp runs the loop (so slot indices and coordinates stay warp-uniform) and one elected lane
+    // issues the copies.  Consecutive tiles of a CTA walk the channel tiles of one token tile, so the
+    // 148 CTAs share a few token tiles in L2 at any time.
+    const bool leader = elect_one();
+    const bool is_x = warp == 0;
+    const int slots = is_x ? GX_SLOTS : GQ_SLOTS;
+    uint64_t* full = is_x ? x_full : q_full;
+    uint64_t* empty = is_x ? x_empty : q_empty;
+    const uint32_t x_panel = static_cast<uint32_t>(nt) * GKB * 2;
+    uint32_t issued = 0, issued_par = 0;
+    for (int idx = 0; idx < total; ++idx) {
+      const int s = idx % slots;
+      const uint32_t ph = (idx / slots) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, abort_flag))) break;
+      const int tile = blockIdx.x + (idx / KT) * gridDim.x;
+      const int kt = idx % KT;
+      if (leader) {
+        if (is_x) {
+          const bool two = args.K - kt * GK > GKB;
+          mbar_arrive_expect_tx(&full[s], two ? 2 * x_panel : x_panel);
+          tma_load_2d(sX + s * G_X_BYTES, &tmX, &full[s], kt * GK, (tile / num_c) * nt);
+          if (two) tma_load_2d(sX + s * G_X_BYTES + G_XSUB_BYTES, &tmX, &full[s], kt * GK + GKB, (tile / num_c) * nt);
         } else {
-          mbar_arrive_expect_tx(&full[s], G_BQ_BYTES);
-          tma_load_2d(sQ + s * G_BQ_BYTES, &tmB, &full[s], kt * GK, (tile % num_n) * GN);
+          // one 128 x 128 box; a half last stage reads zeros past K
+          mbar_arrive_expect_tx(&full[s], G_Q_BYTES);
+          tma_load_2d(sQ + s * G_Q_BYTES, &tmW, &full[s], kt * GK, (tile % num_c) * GW);
         }
-        issued |= 1u << s;
-        issued_par = (issued_par & ~(1u << s)) | (ph << s);
       }
-      // Every issued copy must land before the CTA may exit.
-      for (int i = 0; i < slots; ++i)
-        if (issued & (1u << i)) mbar_wait_drain(&full[i], (issued_par >> i) & 1u);
+      __syncwarp();
+      issued |= 1u << s;
+      issued_par = (issued_par & ~(1u << s)) | (ph << s);
     }
+    // Every issued copy must land before the CTA may exit.
+    for (int i = 0; i < slots; ++i)
+      if (issued & (1u << i)) mbar_wait_drain(&full[i], (issued_par >> i) & 1u);
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = idesc_bf16_f32(UM, GN);
-      int idx = 0;
-      bool ok = true;
-      for (int it = 0; ok && it < my_tiles; ++it) {
-        const int a = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(&tempty[a], aph ^ 1u, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + a * 2 * GN;  // halves at +0 and +GN columns
-        for (int kt = 0; kt < KT; ++kt, ++idx) {
-          const int sa = idx % GA_SLOTS, sh = idx % GH_SLOTS;
-          if (!mbar_wait(&a_full[sa], (idx / GA_SLOTS) & 1, abort_flag) ||
-              !mbar_wait(&h_full[sh], (idx / GH_SLOTS) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t db = sdesc_kmajor_sw128(smem_u32(sH + sh * G_BH_BYTES));
-#pragma unroll
-          for (int mi = 0; mi < GM / UM; ++mi) {
-            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + sa * G_A_BYTES + mi * (G_A_BYTES / 2)));
-#pragma unroll
-            for (int k = 0; k < GK / 16; ++k)
-              mma_f16_ss(d + mi * GN, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0 ? 1u : 0u);
-          }
-          mma_commit(&a_empty[sa]);
-          mma_commit(&h_empty[sh]);
-        }
-        if (!ok) break;
-        mma_commit(&tfull[a]);
-      }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0);
-    }
-  } else if (warp < G_CONV_WARP0) {
-    // -------------------------------------------------------------------- epilogue
-    const int q = warp & 3;                       // TMEM lane quarter this warp may access
-    constexpr int ch = 0;                         // columns handled: the whole tile
-    for (int it = 0; it < my_tiles; ++it) {
-      const int tile = blockIdx.x + it * gridDim.x;
-      const int mb = tile / num_n, nb = tile % num_n;
+    // ------------------------------------------------------------------ MMA issuer
+    // The whole warp runs the loop, so TMEM addresses and smem descriptors are warp-uniform values
+    // (uniform registers feed tcgen05.mma directly); one elected lane issues the tcgen05 ops.
+    const bool leader = elect_one();
+    const uint32_t idesc = idesc_bf16_f32(GW, nt);
+    int idx = 0;
+    bool ok = true;
+    for (int it = 0; ok && it < my_tiles; ++it) {
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tempty[a], aph ^ 1u, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + a * GT;
+      for (int kt = 0; kt < KT; ++kt, ++idx) {
+        const int sx = idx % GX_SLOTS, sw = idx % GW_SLOTS;
+        ok = __all_sync(0xffffffffu, mbar_wait(&x_full[sx], (idx / GX_SLOTS) & 1, abort_flag) &&
+                                         mbar_wait(&w_full[sw], (idx / GW_SLOTS) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t db0 = sdesc_kmajor_sw128(smem_u32(sX + sx * G_X_BYTES));
+        const uint64_t db1 = sdesc_kmajor_sw128(smem_u32(sX + sx * G_X_BYTES + G_XSUB_BYTES));
+        const uint32_t wa = tmem_base + G_W_COL0 + sw * G_W_COLS;
+        const int nk = args.K - kt * GK > GKB ? GK / 16 : GKB / 16;
+        if (leader) {
+#pragma unroll
+          for (int k = 0; k < GK / 16; ++k)
+            if (k < nk)
+              mma_f16_ts(d, wa + k * 8, (k < 4 ? db0 : db1) + 2 * (k & 3), idesc, (kt | k) != 0 ? 1u : 0u);
+          mma_commit(&x_empty[sx]);
+          mma_commit(&w_empty[sw]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (leader) mma_commit(&tfull[a]);
+      __syncwarp();
+    }
+    if (leader) mma_commit(drain);
+    __syncwarp();
+    mbar_wait_drain(drain, 0);
+  } else if (warp < G_CONV_WARP0) {
+    // -------------------------------------------------------------------- epilogue
+    const int q = warp & 3;                  // TMEM lane quarter this warp may access
+    const int eh = (warp - G_EPI_WARP0) >> 2;  // which alternate 32-token chunks
+    const int et = (warp - G_EPI_WARP0) * 32 + lane;
+    const int ch = q * 32 + lane;            // output channel within the tile (= TMEM lane)
+    const float r = args.resid_scale;
+    for (int it = 0; it < my_tiles; ++it) {
+      const int tile = blockIdx.x + it * gridDim.x;
+      const int tb = tile / num_c, cb = tile % num_c;
+      const int a = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const int tok0 = tb * nt;
+      const int n = cb * GW + ch;
       if (MODE == GEMM_RESID32) {
-        // Pull the residual row segments (128 f32 = 512 B per row) of the NEXT tile into L2 while this
-        // one is drained, so their loads hit L2 even when the epilogue is the bottleneck (the first
-        // tile also prefetches its own rows).
-#pragma unroll 1
+        // Pull the residual rows (128 f32 = 512 B per token) of the next tile into L2 while this one
+        // is drained (the first tile also prefetches its own rows).
         for (int pt = (it == 0 ? 0 : 1); pt <= 1; ++pt) {
           if (it + pt >= my_tiles) break;
           const int ptile = blockIdx.x + (it + pt) * gridDim.x;
-          const int pmb = ptile / num_n, pnb = ptile % num_n;
-#pragma unroll
-          for (int mi = 0; mi < GM / UM; ++mi) {
-            const int row = pmb * GM + mi * UM + q * 32 + lane;
-            if (row < args.M) {
-              const char* xr = reinterpret_cast<const char*>(args.resid32 +
-                                                             static_cast<size_t>(row) * args.ld_resid32 + pnb * GN);
-#pragma unroll
-              for (int l2 = 0; l2 < 4; ++l2) prefetch_l2(xr + l2 * 128);
+          const int ptok0 = (ptile / num_c) * nt, pcb = ptile % num_c;
+          for (int l = et; l < nt * 4; l += G_EPI_WARPS * 32) {
+            const int tok = ptok0 + (l >> 2);
+            if (tok < args.M)
+              prefetch_l2(args.resid32 + static_cast<size_t>(tok) * args.ld_resid32 + pcb * GW + (l & 3) * 32);
+          }
+        }
+      }
+      float* rsb = rs_s + a * GT;
+      if (MODE == GEMM_ROWSCALE || MODE == GEMM_SWIGLU) {
+        // per-token rstd of this tile, shared by the epilogue warps; computed before the
+        // accumulator wait so it overlaps the main loop
+        for (int j = et; j < nt; j += G_EPI_WARPS * 32) {
+          const int tok = tok0 + j;
+          float v = 1.0f;
+          if (tok < args.M) {
+            if (args.rowsq) {
+              const float* ps = args.rowsq + static_cast<size_t>(tok) * args.rowsq_ld;
+              float ss = 0.f;
+              for (int p = 0; p < args.rowsq_np; ++p) ss += ps[p];
+              v = rsqrtf(ss * args.inv_norm_dim + args.eps);
+            } else {
+              v = __ldg(args.row_scale + tok);
             }
           }
+          rsb[j] = v;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&esync[a]);
+        if (!mbar_wait(&esync[a], aph, abort_flag)) break;
       }
-      // per-row scalars that do not depend on the accumulator: fetched before waiting for it
-      float rs2[GM / UM];
-#pragma unroll
-      for (int mi = 0; mi < GM / UM; ++mi) {
-        const int row = mb * GM + mi * UM + q * 32 + lane;
-        rs2[mi] = 1.0f;
-        if ((MODE == GEMM_ROWSCALE || MODE == GEMM_SWIGLU) && row < args.M) {
-          if (args.rowsq) {
-            const float* ps = args.rowsq + static_cast<size_t>(row) * args.rowsq_ld;
-            float ss = 0.f;
-            for (int p = 0; p < args.rowsq_np; ++p) ss += ps[p];
-            rs2[mi] = rsqrtf(ss * args.inv_norm_dim + args.eps);
-          } else {
-            rs2[mi] = __ldg(args.row_scale + row);
-          }
-        }
-      }
+      const float cs = __ldg(args.col_scale + n);
       if (!mbar_wait(&tfull[a], aph, abort_flag)) break;
       tc_fence_after();
+      const uint32_t tbase = tmem_base + a * GT + (static_cast<uint32_t>(q * 32) << 16);
+      float* ssb = ss_s + (a * 4 + q) * GT;
+      // RoPE: rows n and n ^ 1 (adjacent lanes) form a rotation pair; rope_cols is a multiple of 32
+      // for the supported head sizes, so the test is uniform across the warp.
+      const bool rope = MODE == GEMM_ROWSCALE && cb * GW + q * 32 < args.rope_cols;
+      const int pj = rope ? (n % args.head_dim) >> 1 : 0;
+      const int hh = args.head_dim >> 1;
 #pragma unroll 1
-      for (int mi = 0; mi < GM / UM; ++mi) {
-        const int row = mb * GM + mi * UM + q * 32 + lane;
-        const bool row_ok = row < args.M;
-        const uint32_t tbase = tmem_base + a * 2 * GN + mi * GN + (static_cast<uint32_t>(q * 32) << 16);
-        const float rs = mi == 0 ? rs2[0] : rs2[1];
-        float sumsq = 0.f;  // RESID32: sum of squares of this row's updated 128-column segment
-        if (MODE == GEMM_SWIGLU) {
-          const int n0 = nb * GN;           // weight rows: [n0, n0+64) gate, [n0+64, n0+128) up
-          const int i0 = nb * (GN / 2);     // output channels
-#pragma unroll 1
-          for (int c0 = 0; c0 < GN / 2; c0 += 16) {
-            uint32_t g[16], u[16];
-            tmem_ld_32x32b_x16(tbase + c0, g);
-            tmem_ld_32x32b_x16(tbase + GN / 2 + c0, u);
-            tmem_ld_wait();
-            if (row_ok) {
-              const float4* sg = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-              const float4* su = reinterpret_cast<const float4*>(args.col_scale + n0 + GN / 2 + c0);
-              uint32_t o[8];
+      for (int c0 = eh * 32; c0 < nt; c0 += 64) {
+        const int tokc = tok0 + c0;
+        const int jn = min(min(32, nt - c0), args.M - tokc);  // valid tokens of the chunk (warp-uniform)
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(tbase + c0, acc);
+        tmem_ld_wait();
+        if (jn <= 0) continue;
+        if (MODE == GEMM_RESID32) {
+          float* xr = args.resid32 + static_cast<size_t>(tokc) * args.ld_resid32 + n;
+          __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
+          float xv[32];
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const float4 a4 = __ldg(sg + v), b4 = __ldg(su + v);
-                const float ga[4] = {a4.x, a4.y, a4.z, a4.w}, ub[4] = {b4.x, b4.y, b4.z, b4.w};
-                float hv[4];
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) xv[j] = xr[static_cast<size_t>(j) * args.ld_resid32];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  hv[e] = silu_f(__uint_as_float(g[4 * v + e]) * rs * ga[e]) *
-                          (__uint_as_float(u[4 * v + e]) * rs * ub[e]);
-                o[2 * v] = pack_bf16x2(hv[0], hv[1]);
-                o[2 * v + 1] = pack_bf16x2(hv[2], hv[3]);
-              }
-              st_global_v8(args.out + static_cast<size_t>(row) * args.ldo + i0 + c0, o[0], o[1], o[2], o[3], o[4],
-                           o[5], o[6], o[7]);
+          for (int j = 0; j < 32; ++j) {
+            const float x = xv[j] + r * (__uint_as_float(acc[j]) * cs);
+            if (j < jn) {
+              xr[static_cast<size_t>(j) * args.ld_resid32] = x;
+              st_global_b16(ob + static_cast<size_t>(j) * args.ldo, x);
+            }
+            xv[j] = j < jn ? x * x : 0.f;
+          }
+          const float ss = warp_transpose_sum32(xv, lane);
+          if (c0 + lane < nt) ssb[c0 + lane] = ss;
+        } else if (MODE == GEMM_SWIGLU) {
+          // even lane = gate row of channel i, odd lane = up row; the even lane outputs the even
+          // token of each pair, the odd lane the odd token
+          const int i = (cb * GW + ch) >> 1;
+          const bool odd = (lane & 1) != 0;
+          __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc + (odd ? 1 : 0)) * args.ldo + i;
+#pragma unroll
+          for (int j4 = 0; j4 < 32; j4 += 4) {
+            const float4 r4 = *reinterpret_cast<const float4*>(rsb + c0 + j4);  // broadcast
+            const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+            for (int h = 0; h < 4; h += 2) {
+              const int j0 = j4 + h;
+              const float x0 = __uint_as_float(acc[j0]) * rr[h] * cs;
+              const float x1 = __uint_as_float(acc[j0 + 1]) * rr[h + 1] * cs;
+              const float recv = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
+              const float g = odd ? recv : x0, u = odd ? x1 : recv;
+              if (j0 + (odd ? 1 : 0) < jn) st_global_b16(ob + static_cast<size_t>(j0) * args.ldo, silu_f(g) * u);
             }
           }
-        } else {
-          const int n0 = nb * GN;
-#pragma unroll 1
-          for (int c0 = 0; c0 < GN; c0 += 32) {
-            uint32_t acc[32];
-            tmem_ld_32x32b_x32(tbase + c0, acc);
-            tmem_ld_wait();
-            if (row_ok && n0 + c0 < args.N) {
-              const float4* sc4 = reinterpret_cast<const float4*>(args.col_scale + n0 + c0);
-              float sc[32];
+        } else if (MODE == GEMM_RESID) {
+          __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
 #pragma unroll
-              for (int v = 0; v < 8; ++v) {
-                const float4 t4 = __ldg(sc4 + v);
-                sc[4 * v] = t4.x;
-                sc[4 * v + 1] = t4.y;
-                sc[4 * v + 2] = t4.z;
-                sc[4 * v + 3] = t4.w;
-              }
-              uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(row) * args.ldo + n0 + c0);
-              uint32_t o[16];
-              if (MODE == GEMM_RESID32) {
-                float* xr = args.resid32 + static_cast<size_t>(row) * args.ld_resid32 + n0 + c0;
-                const float r = args.resid_scale;
-                float xv[4][8];
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) {
+              const float x = __bfloat162float(ob[static_cast<size_t>(j) * args.ldo]);
+              st_global_b16(ob + static_cast<size_t>(j) * args.ldo, x + r * (__uint_as_float(acc[j]) * cs));
+            }
+        } else if (MODE == GEMM_ROWSCALE) {
+          __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
+          if (rope) {
+            const bool odd = (lane & 1) != 0;
+            const int p0 = args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
 #pragma unroll
-                for (int v = 0; v < 4; ++v) ld_global_v8(xr + 8 * v, xv[v]);
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                  float x[8];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) {
-                    x[e] = xv[v][e] + r * (__uint_as_float(acc[8 * v + e]) * sc[8 * v + e]);
-                    sumsq += x[e] * x[e];
-                  }
-                  st_global_v8(xr + 8 * v, __float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]),
-                               __float_as_uint(x[3]), __float_as_uint(x[4]), __float_as_uint(x[5]),
-                               __float_as_uint(x[6]), __float_as_uint(x[7]));
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) o[4 * v + e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
-                }
-              } else if (MODE == GEMM_RESID) {
-                uint4 xin[4];
-#pragma unroll
-                for (int v = 0; v < 4; ++v) xin[v] = dst[v];
-                const uint32_t* xw = reinterpret_cast<const uint32_t*>(xin);
-                const float r = args.resid_scale;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const float2 x = unpack_bf16x2(xw[j]);
-                  o[j] = pack_bf16x2(x.x + r * (__uint_as_float(acc[2 * j]) * sc[2 * j]),
-                                     x.y + r * (__uint_as_float(acc[2 * j + 1]) * sc[2 * j + 1]));
-                }
-              } else if (n0 + c0 < args.rope_cols) {
-                // projection + RoPE on adjacent (x_j, x_{j+hd/2}) pairs, rounded to bf16 once
-                const int pos = args.rope_pos_base + row % args.rope_seq;
-                const float* ct = args.rope_cos + static_cast<size_t>(pos) * (args.head_dim >> 1);
-                const float* st = args.rope_sin + static_cast<size_t>(pos) * (args.head_dim >> 1);
-                // head-local column of this 32-column chunk; a chunk crosses at most one head boundary
-                const int hl0 = (n0 + c0) % args.head_dim;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  int hl = hl0 + 2 * j;
-                  hl = hl >= args.head_dim ? hl - args.head_dim : hl;
-                  const int pj = hl >> 1;
-                  const float c = __ldg(ct + pj), sn = __ldg(st + pj);
-                  const float xa = __uint_as_float(acc[2 * j]) * rs * sc[2 * j];
-                  const float xb = __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1];
-                  o[j] = pack_bf16x2(xa * c - xb * sn, xb * c + xa * sn);
-                }
+            for (int j = 0; j < 32; ++j) {
+              int pos;
+              if (args.rope_seq >= 32) {
+                pos = p0 + j;
+                pos = pos >= args.rope_seq ? pos - args.rope_seq : pos;
               } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                  o[j] = pack_bf16x2(__uint_as_float(acc[2 * j]) * rs * sc[2 * j],
-                                     __uint_as_float(acc[2 * j + 1]) * rs * sc[2 * j + 1]);
+                pos = (tokc + j) % args.rope_seq;
               }
-              st_global_v8(dst, o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7]);
-              st_global_v8(dst + 2, o[8], o[9], o[10], o[11], o[12], o[13], o[14], o[15]);
+              pos += args.rope_pos_base;
+              const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
+              const float y = __shfl_xor_sync(0xffffffffu, x, 1);
+              if (j < jn) {
+                const float c = __ldg(args.rope_cos + static_cast<size_t>(pos) * hh + pj);
+                const float sn = __ldg(args.rope_sin + static_cast<size_t>(pos) * hh + pj);
+                // even lane: (x_a, x_b) = (x, y) -> x_a c - x_b s; odd lane: (x_a, x_b) = (y, x) -> x_b c + x_a s
+                st_global_b16(ob + static_cast<size_t>(j) * args.ldo, odd ? x * c + y * sn : x * c - y * sn);
+              }
             }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < jn)
+                st_global_b16(ob + static_cast<size_t>(j) * args.ldo, __uint_as_float(acc[j]) * rsb[c0 + j] * cs);
           }
-          if (MODE == GEMM_RESID32 && args.rowsq && row_ok)
-            args.rowsq[static_cast<size_t>(row) * args.rowsq_ld + nb] = sumsq;
+        } else {  // COLSCALE
+          __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) st_global_b16(ob + static_cast<size_t>(j) * args.ldo, __uint_as_float(acc[j]) * cs);
         }
       }
+      // accumulator drained: the MMAs of tile it + 2 may overwrite it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[a]);
+      if (MODE == GEMM_RESID32 && args.rowsq) {
+        // combine the four lane quarters' partial sums per token (fixed order) into the tile's statistic
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&esync[a]);
+        if (!mbar_wait(&esync[a], aph, abort_flag)) break;
+        const float* s0 = ss_s + a * 4 * GT;
+        for (int j = et; j < nt; j += G_EPI_WARPS * 32) {
+          const int tok = tok0 + j;
+          if (tok < args.M)
+            args.rowsq[static_cast<size_t>(tok) * args.rowsq_ld + cb] =
+                ((s0[j] + s0[GT + j]) + s0[2 * GT + j]) + s0[3 * GT + j];
+        }
+      }
     }
   } else {
     // -------------------------------------------------------------------- int8 -> bf16 converters
-    const int ct = threadIdx.x - G_CONV_WARP0 * 32;  // 0..255
+    // Thread = one weight row (output channel) of the tile, half of the stage's 128 K values.
+    // Weight tiles arrive 128B-swizzled: 16-byte chunk c of row rr sits at rr*128 + ((c ^ (rr&7))<<4),
+    // so the eight rows of each quarter-warp phase hit distinct banks.
+    constexpr int CPT = (GK / 16) / (G_CONV_WARPS / 4);    // 16-byte chunks of the row per thread
+    const int cq = warp & 3;                               // TMEM lane quarter
+    const int kh = (warp - G_CONV_WARP0) >> 2;             // which part of the k-step
+    const int rr = cq * 32 + lane;                         // weight row within the tile
+    const uint32_t xsw = rr & 7;
+    const uint32_t toff = static_cast<uint32_t>(cq * 32) << 16;
     for (int idx = 0; idx < total; ++idx) {
-      const int sq = idx % GQ_SLOTS, sh = idx % GH_SLOTS;
+      const int sq = idx % GQ_SLOTS, sw = idx % GW_SLOTS;
       if (!mbar_wait(&q_full[sq], (idx / GQ_SLOTS) & 1, abort_flag)) break;
-      const uint8_t* bq = sQ + sq * G_BQ_BYTES;
-      uint4 v[(GN * GK / 16) / (G_CONV_WARPS * 32)];
+      const uint8_t* rowp = sQ + sq * G_Q_BYTES + rr * GK;
+      uint4 v[CPT];
 #pragma unroll
-      for (int i = 0; i < (GN * GK / 16) / (G_CONV_WARPS * 32); ++i) {
-        const int c = ct + i * G_CONV_WARPS * 32;
-        v[i] = *reinterpret_cast<const uint4*>(bq + (c >> 2) * GK + (c & 3) * 16);
-      }
-      if (!mbar_wait(&h_empty[sh], ((idx / GH_SLOTS) & 1) ^ 1u, abort_flag)) break;
-      uint8_t* bh = sH + sh * G_BH_BYTES;
+      for (int c = 0; c < CPT; ++c) v[c] = *reinterpret_cast<const uint4*>(rowp + (((kh * CPT + c) ^ xsw) << 4));
+      uint32_t o[8 * CPT];
 #pragma unroll
-      for (int i = 0; i < (GN * GK / 16) / (G_CONV_WARPS * 32); ++i) {
-        const int c = ct + i * G_CONV_WARPS * 32;  // 16-byte chunk of the int8 tile
-        const int n = c >> 2, kc = c & 3;
-        uint4 o0, o1;
-        i8x4_to_bf16x4(v[i].x, o0.x, o0.y);
-        i8x4_to_bf16x4(v[i].y, o0.z, o0.w);
-        i8x4_to_bf16x4(v[i].z, o1.x, o1.y);
-        i8x4_to_bf16x4(v[i].w, o1.z, o1.w);
-        const int sw = n & 7;
-        uint8_t* rowp = bh + n * 128;
-        *reinterpret_cast<uint4*>(rowp + (((2 * kc) ^ sw) << 4)) = o0;
-        *reinterpret_cast<uint4*>(rowp + (((2 * kc + 1) ^ sw) << 4)) = o1;
+      for (int c = 0; c < CPT; ++c) {
+        i8x4_to_bf16x4(v[c].x, o[8 * c + 0], o[8 * c + 1]);
+        i8x4_to_bf16x4(v[c].y, o[8 * c + 2], o[8 * c + 3]);
+        i8x4_to_bf16x4(v[c].z, o[8 * c + 4], o[8 * c + 5]);
+        i8x4_to_bf16x4(v[c].w, o[8 * c + 6], o[8 * c + 7]);
       }
-      fence_proxy_async_smem();
+      // Every lane has consumed its loaded bytes (the conversion used them), so the TMA may now
+      // overwrite the slot.  Releasing it right after issuing the loads let a refill race them.
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&q_empty[sq]);  // int8 slot consumed (its values were used above): may be refilled
-        mbar_arrive(&h_full[sh]);
-      }
+      if (lane == 0) mbar_arrive(&q_empty[sq]);
+      if (!mbar_wait(&w_empty[sw], ((idx / GW_SLOTS) & 1) ^ 1u, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t ta = tmem_base + toff + G_W_COL0 + sw * G_W_COLS + kh * 8 * CPT;  // 8 columns per chunk
+      if constexpr (CPT == 4)
+        tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
+      else
+        tmem_st_32x32b_x16(ta, *reinterpret_cast<const uint32_t(*)[16]>(o));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&w_full[sw]);
     }
   }
 

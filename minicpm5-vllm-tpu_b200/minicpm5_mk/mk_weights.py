@@ -10,10 +10,10 @@ the parts this path keeps, re-laid-out for the tcgen05 GEMMs:
   q = clamp(round_half_even(W / scale), -127, 127) (`_quantize_w`, `mk_weights.py:113-123`).
   No activation quantisation (the reference's W8A8 SmoothQuant calibration is not used).
 * Every projection stays [out_features, in_features] (K contiguous = "K-major" B operand).
-* gate/up are fused into one [2I, H] matrix interleaved in blocks of GU_BLOCK rows
-  ([g_0..g_63, u_0..u_63, g_64..g_127, u_64..]) so each 128-row GEMM tile holds matching gate and
-  up channels and SiLU(g)*u is tile-local in the epilogue (same idea as the reference's
-  chunk-interleaved `interleave_gu`, `plugin/minicpm5_mk/mk_mlp.py:148-158`).
+* gate/up are fused into one [2I, H] matrix with alternating rows ([g_0, u_0, g_1, u_1, ...],
+  GU_BLOCK = 1): the GEMM keeps one weight row per TMEM lane, so gate and up of a channel sit in
+  adjacent lanes and SiLU(g)*u takes one lane shuffle in the epilogue (same idea as the reference's
+  chunk-interleaved `interleave_gu`, `plugin/minicpm5_mk/mk_mlp.py:148-158`, at a block of 1).
 * All L layers are int8 (the reference keeps its last layer in bf16 because W8A8 hurt accuracy;
   weight-only int8 does not need that).
 * RoPE tables: inv_freq = theta^(-2i/hd) and angles in float64, cos/sin stored as f32
@@ -33,7 +33,7 @@ import torch
 
 from .mk_config import MkConfig
 
-GU_BLOCK = 64
+GU_BLOCK = 1
 BF16 = torch.bfloat16
 F32 = torch.float32
 

@@ -46,7 +46,8 @@ def _rope_pairs(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.
     return bf(out)
 
 
-def _deinterleave(t: torch.Tensor, block: int = 64):
+def _deinterleave(t: torch.Tensor, block: int = 1):
+    """Fused gate/up rows of the prepared weights (alternating rows) -> (gate, up)."""
     n2 = t.shape[0]
     v = t.reshape(n2 // (2 * block), 2, block, *t.shape[1:])
     return v[:, 0].reshape(n2 // 2, *t.shape[1:]), v[:, 1].reshape(n2 // 2, *t.shape[1:])

@@ -51,8 +51,12 @@ def test_gu_interleave_roundtrip():
     g = torch.arange(512 * 3).reshape(512, 3)
     u = -g
     x = mk_weights.interleave_gu(g, u)
-    assert torch.equal(x[:64], g[:64]) and torch.equal(x[64:128], u[:64])
+    assert torch.equal(x[0::2], g) and torch.equal(x[1::2], u)  # row 2i = gate i, row 2i+1 = up i
     g2, u2 = mk_weights.deinterleave_gu(x)
+    assert torch.equal(g2, g) and torch.equal(u2, u)
+    x64 = mk_weights.interleave_gu(g, u, block=64)
+    assert torch.equal(x64[:64], g[:64]) and torch.equal(x64[64:128], u[:64])
+    g2, u2 = mk_weights.deinterleave_gu(x64, block=64)
     assert torch.equal(g2, g) and torch.equal(u2, u)
 
 
