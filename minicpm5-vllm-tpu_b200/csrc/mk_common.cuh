@@ -286,30 +286,27 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) { return idesc_bf16_f32(M, N) | (1u << 16); }
 
 // ---------------------------------------------------------------------------------- numerics
-// Four signed int8 (one 32-bit word) -> four bf16 (two 32-bit words), exact.
-// Each byte is biased to u = x + 128 and placed in the mantissa of 2^23 (0x4B0000uu), so the f32
-// value is 2^23 + u; subtracting 2^23 + 128 (two lanes at a time with the packed f32x2 add) leaves x
-// exactly.  |x| <= 128 needs 8 significant bits, so the upper 16 bits of each f32 are the exact bf16.
+// Four signed int8 (one 32-bit word) -> four bf16 (two 32-bit words), exact; lo = (x0, x1),
+// hi = (x2, x3), lower K in the low half.
+// Each byte b goes into the low byte of a 16-bit lane under 0x43 (the bf16 exponent of 128).  With
+// bit 7 cleared the lane is bf16(128 + (b & 0x7F)); the two's-complement value is
+// x = (b & 0x7F) - 128 * b7 = that - 128 - 128 * b7, so one bf16x2 add of c = bf16(-128) or
+// bf16(-256) (0xC300 with bit 7 of b copied in) gives x.  Every operand and the sum are integers of
+// at most 8 significant bits, so the add is exact.  8 instructions per 4 values.
 __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
   asm("{\n\t"
-      ".reg .b32 u, a0, a1, a2, a3;\n\t"
-      ".reg .b64 p0, p1;\n\t"
-      "xor.b32 u, %2, 0x80808080;\n\t"
-      "prmt.b32 a0, u, 0x4B000000, 0x7540;\n\t"
-      "prmt.b32 a1, u, 0x4B000000, 0x7541;\n\t"
-      "prmt.b32 a2, u, 0x4B000000, 0x7542;\n\t"
-      "prmt.b32 a3, u, 0x4B000000, 0x7543;\n\t"
-      "mov.b64 p0, {a0, a1};\n\t"
-      "mov.b64 p1, {a2, a3};\n\t"
-      "add.rn.f32x2 p0, p0, %3;\n\t"
-      "add.rn.f32x2 p1, p1, %3;\n\t"
-      "mov.b64 {a0, a1}, p0;\n\t"
-      "mov.b64 {a2, a3}, p1;\n\t"
-      "prmt.b32 %0, a0, a1, 0x7632;\n\t"
-      "prmt.b32 %1, a2, a3, 0x7632;\n\t"
+      ".reg .b32 r0, r1, v0, v1, c0, c1;\n\t"
+      "prmt.b32 r0, %2, 0x43434343, 0x4140;\n\t"             // [b0, 0x43, b1, 0x43]
+      "prmt.b32 r1, %2, 0x43434343, 0x4342;\n\t"             // [b2, 0x43, b3, 0x43]
+      "and.b32 v0, r0, 0xFF7FFF7F;\n\t"
+      "and.b32 v1, r1, 0xFF7FFF7F;\n\t"
+      "lop3.b32 c0, r0, 0x00800080, 0xC300C300, 0xEA;\n\t"   // (r & 0x80) | 0xC300 per lane
+      "lop3.b32 c1, r1, 0x00800080, 0xC300C300, 0xEA;\n\t"
+      "add.rn.bf16x2 %0, v0, c0;\n\t"
+      "add.rn.bf16x2 %1, v1, c1;\n\t"
       "}"
       : "=r"(lo), "=r"(hi)
-      : "r"(w), "l"(0xCB000080CB000080ull));  // (-(2^23 + 128), -(2^23 + 128)) as f32 pairs
+      : "r"(w));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
