@@ -11,7 +11,8 @@
 //
 //   warp 0      TMA producer: Q0/Q1 once (3D map over [token, head, dim], 128B swizzle), then a
 //               2-stage ring of K and V tiles (K: K-major operand; V: MN-major operand)
-//   warp 1      TMEM allocator + single-thread MMA issuer.  For 64-key tile j it issues
+//   warp 1      TMEM allocator + MMA issuer (warp-wide loop, one elected lane issues).  For
+//               64-key tile j it issues
 //                 S_t(j+1) = Q_t K_{j+1}^T into the other S buffer of tile t  (M=128, N=64, K=hd)
 //                 O_t += P_t(j) V_j  once the softmax has written P_t(j)        (M=128, N=hd, K=64)
 //               so the tensor core computes the next scores while the softmax works on this tile;
@@ -113,45 +114,54 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- TMA producer
-      uint32_t issued = 0, issued_par = 0;  // bit s: stage s has loads in flight / their parity
+    // ---------------------------------------------------------------- TMA producer
+    // The whole warp runs the loop (warp-uniform addresses); one elected lane issues the copies.
+    const bool leader = elect_one();
+    uint32_t issued = 0, issued_par = 0;  // bit s: stage s has loads in flight / their parity
+    if (leader) {
       mbar_arrive_expect_tx(q_full, 4 * TA_QCHUNK);
       for (int t = 0; t < 2; ++t)
         for (int c = 0; c < 2; ++c)
           tma_load_3d(sQ + (t * 2 + c) * TA_QCHUNK, &tmQ, q_full, c * 64, g * G, tok0 + q0 + t * qpt);
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % TA_STAGES;
-        const uint32_t ph = (j / TA_STAGES) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag)) break;
-        uint8_t* sst = sKV + st * TA_STAGE;
+    }
+    __syncwarp();
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % TA_STAGES;
+      const uint32_t ph = (j / TA_STAGES) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag))) break;
+      uint8_t* sst = sKV + st * TA_STAGE;
+      if (leader) {
         mbar_arrive_expect_tx(&k_full[st], 2 * TA_KCHUNK);
         for (int c = 0; c < 2; ++c) tma_load_3d(sst + c * TA_KCHUNK, &tmK, &k_full[st], c * 64, g, tok0 + j * TA_BK);
         mbar_arrive_expect_tx(&v_full[st], 2 * TA_KCHUNK);
         for (int c = 0; c < 2; ++c)
           tma_load_3d(sst + (2 + c) * TA_KCHUNK, &tmV, &v_full[st], c * 64, g, tok0 + j * TA_BK);
-        issued |= 1u << st;
-        issued_par = (issued_par & ~(1u << st)) | (ph << st);
       }
-      // every issued copy must land before the CTA exits
-      mbar_wait_drain(q_full, 0);
-      for (int st = 0; st < TA_STAGES; ++st)
-        if (issued & (1u << st)) {
-          mbar_wait_drain(&k_full[st], (issued_par >> st) & 1u);
-          mbar_wait_drain(&v_full[st], (issued_par >> st) & 1u);
-        }
+      __syncwarp();
+      issued |= 1u << st;
+      issued_par = (issued_par & ~(1u << st)) | (ph << st);
     }
+    // every issued copy must land before the CTA exits
+    mbar_wait_drain(q_full, 0);
+    for (int st = 0; st < TA_STAGES; ++st)
+      if (issued & (1u << st)) {
+        mbar_wait_drain(&k_full[st], (issued_par >> st) & 1u);
+        mbar_wait_drain(&v_full[st], (issued_par >> st) & 1u);
+      }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, TA_BK);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32_bmn(128, HD);
-      // S_t(j) = Q_t K_j^T into S buffer j & 1 of tile t
-      auto issue_s = [&](int j) {
-        const int st = j % TA_STAGES;
-        const uint8_t* kb = sKV + st * TA_STAGE;
-        for (int t = 0; t < 2; ++t) {
-          const uint32_t d = tmem + t * 128 + (j & 1) * 64;
+    // ---------------------------------------------------------------- MMA issuer
+    // The whole warp runs the loop, so TMEM addresses and smem descriptors are warp-uniform
+    // (uniform registers feed tcgen05.mma directly); one elected lane issues the tcgen05 ops.
+    const bool leader = elect_one();
+    constexpr uint32_t idesc_s = idesc_bf16_f32(128, TA_BK);
+    constexpr uint32_t idesc_pv = idesc_bf16_f32_bmn(128, HD);
+    // S_t(j) = Q_t K_j^T into S buffer j & 1 of tile t
+    auto issue_s = [&](int j) {
+      const int st = j % TA_STAGES;
+      const uint8_t* kb = sKV + st * TA_STAGE;
+      for (int t = 0; t < 2; ++t) {
+        const uint32_t d = tmem + t * 128 + (j & 1) * 64;
+        if (leader) {
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
             const int c = ks >> 2;
@@ -161,34 +171,37 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           }
           mma_commit(&s_full[t * 2 + (j & 1)]);
         }
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
+        __syncwarp();
       }
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % TA_STAGES;
-        if (j + 1 < ntiles) {
-          const int j1 = j + 1;
-          if (!mbar_wait(&k_full[j1 % TA_STAGES], (j1 / TA_STAGES) & 1, abort_flag)) break;
-          // S buffer (j+1)&1 still holds P_t(j-1), read by O_t += P_t(j-1) V.  tcgen05.mma ops issued
-          // by this thread execute in issue order, so S_t(j+1) (issued after that P V) overwrites P_t(j-1)
-          // only after it has been read: no wait, the tensor pipe stays full.  The softmax finished
-          // reading S_t(j-1) before it signalled p_ready for tile j-1, which this thread consumed.
-          tc_fence_after();
-          issue_s(j1);
+    };
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag));
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+    }
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int st = j % TA_STAGES;
+      if (j + 1 < ntiles) {
+        const int j1 = j + 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[j1 % TA_STAGES], (j1 / TA_STAGES) & 1, abort_flag))) break;
+        // S buffer (j+1)&1 still holds P_t(j-1), read by O_t += P_t(j-1) V.  tcgen05.mma ops issued
+        // by this thread execute in issue order, so S_t(j+1) (issued after that P V) overwrites P_t(j-1)
+        // only after it has been read: no wait, the tensor pipe stays full.  The softmax finished
+        // reading S_t(j-1) before it signalled p_ready for tile j-1, which this thread consumed.
+        tc_fence_after();
+        issue_s(j1);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag))) break;
+      const uint32_t vb = smem_u32(sKV + st * TA_STAGE + 2 * TA_KCHUNK);
+      for (int t = 0; t < 2; ++t) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
         }
-        if (!mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag)) break;
-        const uint32_t vb = smem_u32(sKV + st * TA_STAGE + 2 * TA_KCHUNK);
-        for (int t = 0; t < 2; ++t) {
-          if (!mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + 256 + t * 128;
-          const uint32_t pa = tmem + t * 128 + (j & 1) * 64;
+        tc_fence_after();
+        const uint32_t d = tmem + 256 + t * 128;
+        const uint32_t pa = tmem + t * 128 + (j & 1) * 64;
+        if (leader) {
 #pragma unroll
           for (int ks = 0; ks < TA_BK / 16; ++ks) {
             const uint64_t db = sdesc_mnmajor_sw128(vb + ks * 2048, TA_KCHUNK);
@@ -196,12 +209,15 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           }
           mma_commit(&pv_done[t]);
         }
-        if (!ok) break;
-        mma_commit(&kv_empty[st]);
+        __syncwarp();
       }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      if (!ok) break;
+      if (leader) mma_commit(&kv_empty[st]);
+      __syncwarp();
     }
+    if (leader) mma_commit(drain);
+    __syncwarp();
+    mbar_wait_drain(drain, 0);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ softmax + epilogue
     const int t = (warp - 4) >> 2;
