@@ -332,6 +332,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (!mbar_wait(&esync[a], aph, abort_flag)) break;
       }
       const float cs = __ldg(args.col_scale + n);
+      // RESID32: the residual values of the warp's next chunk are loaded one chunk ahead (the first
+      // before the accumulator wait), so their latency overlaps TMEM reads and the reduction.
+      float xv[32];
+      auto load_resid = [&](int c0) {
+        const int jn = min(min(32, nt - c0), args.M - (tok0 + c0));
+        const float* xr = args.resid32 + static_cast<size_t>(tok0 + c0) * args.ld_resid32 + n;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < jn) xv[j] = xr[static_cast<size_t>(j) * args.ld_resid32];
+      };
+      if (MODE == GEMM_RESID32 && eh * 32 < nt) load_resid(eh * 32);
       if (!mbar_wait(&tfull[a], aph, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + a * GT + (static_cast<uint32_t>(q * 32) << 16);
@@ -352,10 +363,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (MODE == GEMM_RESID32) {
           float* xr = args.resid32 + static_cast<size_t>(tokc) * args.ld_resid32 + n;
           __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
-          float xv[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < jn) xv[j] = xr[static_cast<size_t>(j) * args.ld_resid32];
+          float sq[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float x = xv[j] + r * (__uint_as_float(acc[j]) * cs);
@@ -363,9 +371,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               xr[static_cast<size_t>(j) * args.ld_resid32] = x;
               st_global_b16(ob + static_cast<size_t>(j) * args.ldo, x);
             }
-            xv[j] = j < jn ? x * x : 0.f;
+            sq[j] = j < jn ? x * x : 0.f;
           }
-          const float ss = warp_transpose_sum32(xv, lane);
+          if (c0 + 64 < nt) load_resid(c0 + 64);
+          const float ss = warp_transpose_sum32(sq, lane);
           if (c0 + lane < nt) ssb[c0 + lane] = ss;
         } else if (MODE == GEMM_SWIGLU) {
           // even lane = gate row of channel i, odd lane = up row; the even lane outputs the even
