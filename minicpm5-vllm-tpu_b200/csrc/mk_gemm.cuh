@@ -409,23 +409,34 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if (rope) {
             const bool odd = (lane & 1) != 0;
             const int p0 = args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
+            // Table entries for 8 tokens are loaded back to back before they are used (unconditional
+            // loads, invalid tokens read token 0's entry), so their latency is paid once per 8 tokens.
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              int pos;
-              if (args.rope_seq >= 32) {
-                pos = p0 + j;
-                pos = pos >= args.rope_seq ? pos - args.rope_seq : pos;
-              } else {
-                pos = (tokc + j) % args.rope_seq;
+            for (int hb = 0; hb < 32; hb += 8) {
+              float cv[8], sv[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const int j = hb + jj < jn ? hb + jj : 0;
+                int pos;
+                if (args.rope_seq >= 32) {
+                  pos = p0 + j;
+                  pos = pos >= args.rope_seq ? pos - args.rope_seq : pos;
+                } else {
+                  pos = (tokc + j) % args.rope_seq;
+                }
+                const size_t e = static_cast<size_t>(pos + args.rope_pos_base) * hh + pj;
+                cv[jj] = __ldg(args.rope_cos + e);
+                sv[jj] = __ldg(args.rope_sin + e);
               }
-              pos += args.rope_pos_base;
-              const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
-              const float y = __shfl_xor_sync(0xffffffffu, x, 1);
-              if (j < jn) {
-                const float c = __ldg(args.rope_cos + static_cast<size_t>(pos) * hh + pj);
-                const float sn = __ldg(args.rope_sin + static_cast<size_t>(pos) * hh + pj);
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const int j = hb + jj;
+                const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
+                const float y = __shfl_xor_sync(0xffffffffu, x, 1);
                 // even lane: (x_a, x_b) = (x, y) -> x_a c - x_b s; odd lane: (x_a, x_b) = (y, x) -> x_b c + x_a s
-                st_global_b16(ob + static_cast<size_t>(j) * args.ldo, odd ? x * c + y * sn : x * c - y * sn);
+                if (j < jn)
+                  st_global_b16(ob + static_cast<size_t>(j) * args.ldo,
+                                odd ? x * cv[jj] + y * sv[jj] : x * cv[jj] - y * sv[jj]);
               }
             }
           } else {
