@@ -409,34 +409,52 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if (rope) {
             const bool odd = (lane & 1) != 0;
             const int p0 = args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
-            // Table entries for 8 tokens are loaded back to back before they are used (unconditional
-            // loads, invalid tokens read token 0's entry), so their latency is paid once per 8 tokens.
+            if (args.rope_seq >= 32 && p0 + 32 <= args.rope_seq) {
+              // The chunk's 32 tokens have consecutive positions: (cos, sin) of the pair's angle at
+              // each position follow from the previous one by the angle-addition rotation with the
+              // one-position step (the table's position-1 entry).  The table is re-read every 8 tokens,
+              // so at most 7 rotations (a few f32 ulps) separate any value from a table entry.
+              const float ct = __ldg(args.rope_cos + hh + pj), st = __ldg(args.rope_sin + hh + pj);
 #pragma unroll
-            for (int hb = 0; hb < 32; hb += 8) {
-              float cv[8], sv[8];
+              for (int hb = 0; hb < 32; hb += 8) {
+                const size_t e = static_cast<size_t>(p0 + hb + args.rope_pos_base) * hh + pj;
+                float c = __ldg(args.rope_cos + e), sn = __ldg(args.rope_sin + e);
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                const int j = hb + jj < jn ? hb + jj : 0;
-                int pos;
-                if (args.rope_seq >= 32) {
-                  pos = p0 + j;
-                  pos = pos >= args.rope_seq ? pos - args.rope_seq : pos;
-                } else {
-                  pos = (tokc + j) % args.rope_seq;
+                for (int jj = 0; jj < 8; ++jj) {
+                  const int j = hb + jj;
+                  const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
+                  const float y = __shfl_xor_sync(0xffffffffu, x, 1);
+                  // even lane: (x_a, x_b) = (x, y) -> x_a c - x_b s; odd lane: (x_a, x_b) = (y, x) -> x_b c + x_a s
+                  if (j < jn)
+                    st_global_b16(ob + static_cast<size_t>(j) * args.ldo, odd ? x * c + y * sn : x * c - y * sn);
+                  const float c1 = c * ct - sn * st;
+                  sn = sn * ct + c * st;
+                  c = c1;
                 }
-                const size_t e = static_cast<size_t>(pos + args.rope_pos_base) * hh + pj;
-                cv[jj] = __ldg(args.rope_cos + e);
-                sv[jj] = __ldg(args.rope_sin + e);
               }
+            } else {
+              // positions wrap inside the chunk (short sequences, or one position per row): per-token
+              // table entries, loaded 4 tokens at a time before use
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                const int j = hb + jj;
-                const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
-                const float y = __shfl_xor_sync(0xffffffffu, x, 1);
-                // even lane: (x_a, x_b) = (x, y) -> x_a c - x_b s; odd lane: (x_a, x_b) = (y, x) -> x_b c + x_a s
-                if (j < jn)
-                  st_global_b16(ob + static_cast<size_t>(j) * args.ldo,
-                                odd ? x * cv[jj] + y * sv[jj] : x * cv[jj] - y * sv[jj]);
+              for (int hb = 0; hb < 32; hb += 4) {
+                float cv[4], sv[4];
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                  const int j = hb + jj < jn ? hb + jj : 0;
+                  const int pos = (tokc + j) % args.rope_seq;
+                  const size_t e = static_cast<size_t>(pos + args.rope_pos_base) * hh + pj;
+                  cv[jj] = __ldg(args.rope_cos + e);
+                  sv[jj] = __ldg(args.rope_sin + e);
+                }
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                  const int j = hb + jj;
+                  const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
+                  const float y = __shfl_xor_sync(0xffffffffu, x, 1);
+                  if (j < jn)
+                    st_global_b16(ob + static_cast<size_t>(j) * args.ldo,
+                                  odd ? x * cv[jj] + y * sv[jj] : x * cv[jj] - y * sv[jj]);
+                }
               }
             }
           } else {
