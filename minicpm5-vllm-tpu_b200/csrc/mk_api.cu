@@ -18,7 +18,6 @@
 
 namespace {
 
-using mk::AttnArgs;
 using mk::AttnLastArgs;
 using mk::GemmArgs;
 
@@ -74,10 +73,6 @@ mk_status device_state(DeviceState** out) {
                     mk::gemm_w8a16_kernel<MK_GEMM_RESID32>})
       MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(mk::G_SMEM_BYTES)));
-    MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::AttnShape<96>::SMEM)));
-    MK_CUDA(cudaFuncSetAttribute(mk::attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::AttnShape<128>::SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::TA_SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -239,32 +234,6 @@ mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int 
     mk::attn_tc_kernel<96><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
   else
     mk::attn_tc_kernel<128><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
-  return cuda_status(cudaGetLastError());
-}
-
-// mma.sync attention (mk_attn.cuh), kept as the reference point of the first version.
-mk_status launch_attn_mma(const DeviceState*, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
-                          int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
-  const int G = n_q / n_kv;
-  const int BQ = 16 * (8 / G);
-  AttnArgs a;
-  a.S = S;
-  a.n_q = n_q;
-  a.n_kv = n_kv;
-  a.ld_qkv = ld_qkv;
-  a.q_col = q_col;
-  a.k_col = k_col;
-  a.v_col = v_col;
-  a.ld_out = ld_out;
-  a.scale_log2 = scale_log2;
-  a.nqb = S / BQ;
-  dim3 grid(a.nqb, n_kv, bs);
-  const auto* q = static_cast<const __nv_bfloat16*>(qkv);
-  auto* o = static_cast<__nv_bfloat16*>(out);
-  if (hd == 96)
-    mk::attn_prefill_kernel<96><<<grid, mk::ATT_THREADS, mk::AttnShape<96>::SMEM, st>>>(q, o, a);
-  else
-    mk::attn_prefill_kernel<128><<<grid, mk::ATT_THREADS, mk::AttnShape<128>::SMEM, st>>>(q, o, a);
   return cuda_status(cudaGetLastError());
 }
 
