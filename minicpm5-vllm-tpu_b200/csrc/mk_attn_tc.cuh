@@ -7,12 +7,12 @@
 //
 // One CTA = one KV head g of one sequence x one block of queries.  The G = n_q / n_kv query heads
 // of the group are stacked with the queries into 128-row tiles (row r = query r / G, head r % G);
-// the CTA owns two such tiles (Q0, Q1) that share each 128-key K/V tile:
+// the CTA owns two such tiles (Q0, Q1) that share each 64-key K/V tile:
 //
 //   warp 0      TMA producer: Q0/Q1 once (3D map over [token, head, dim], 128B swizzle), then a
-//               2-stage ring of K and V tiles (K: K-major operand; V: MN-major operand)
-//   warp 1      TMEM allocator + MMA issuer (warp-wide loop, one elected lane issues).  For
-//               64-key tile j it issues
+//               4-stage ring of K and V tiles (K: K-major operand; V: MN-major operand)
+//   warps 1, 2  MMA issuers, one per query tile (warp 1 also allocates TMEM); each runs its loop
+//               warp-wide and one elected lane issues.  For 64-key tile j it issues
 //                 S_t(j+1) = Q_t K_{j+1}^T into the other S buffer of tile t  (M=128, N=64, K=hd)
 //                 O_t += P_t(j) V_j  once the softmax has written P_t(j)        (M=128, N=hd, K=64)
 //               so the tensor core computes the next scores while the softmax works on this tile;
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     for (int i = 0; i < TA_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);  // one commit per MMA issuer
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     }
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -148,31 +148,33 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         mbar_wait_drain(&k_full[st], (issued_par >> st) & 1u);
         mbar_wait_drain(&v_full[st], (issued_par >> st) & 1u);
       }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    // The whole warp runs the loop, so TMEM addresses and smem descriptors are warp-uniform
-    // (uniform registers feed tcgen05.mma directly); one elected lane issues the tcgen05 ops.
+  } else if (warp == 1 || warp == 2) {
+    // ---------------------------------------------------------------- MMA issuers
+    // Warp 1 issues the UMMAs of query tile 0, warp 2 those of tile 1: a single issuing thread
+    // needs about 50 cycles per UMMA, more than a 64-key S UMMA takes to execute, so one issuer
+    // per tile keeps the tensor pipe fed.  The two touch disjoint TMEM (S_t, P_t, O_t) and only
+    // read the shared K/V stages; each waits for the same K/V barriers and releases a stage with its
+    // own commit (kv_empty counts two).  Each whole warp runs its loop (warp-uniform descriptors) and
+    // one elected lane issues.
+    const int t = warp - 1;
     const bool leader = elect_one();
     constexpr uint32_t idesc_s = idesc_bf16_f32(128, TA_BK);
     constexpr uint32_t idesc_pv = idesc_bf16_f32_bmn(128, HD);
     // S_t(j) = Q_t K_j^T into S buffer j & 1 of tile t
     auto issue_s = [&](int j) {
-      const int st = j % TA_STAGES;
-      const uint8_t* kb = sKV + st * TA_STAGE;
-      for (int t = 0; t < 2; ++t) {
-        const uint32_t d = tmem + t * 128 + (j & 1) * 64;
-        if (leader) {
+      const uint8_t* kb = sKV + (j % TA_STAGES) * TA_STAGE;
+      const uint32_t d = tmem + t * 128 + (j & 1) * 64;
+      if (leader) {
 #pragma unroll
-          for (int ks = 0; ks < HD / 16; ++ks) {
-            const int c = ks >> 2;
-            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_QCHUNK)) + 2 * (ks & 3);
-            const uint64_t db = sdesc_kmajor_sw128(smem_u32(kb + c * TA_KCHUNK)) + 2 * (ks & 3);
-            mma_f16_ss(d, da, db, idesc_s, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[t * 2 + (j & 1)]);
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const int c = ks >> 2;
+          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_QCHUNK)) + 2 * (ks & 3);
+          const uint64_t db = sdesc_kmajor_sw128(smem_u32(kb + c * TA_KCHUNK)) + 2 * (ks & 3);
+          mma_f16_ss(d, da, db, idesc_s, ks > 0 ? 1u : 0u);
         }
-        __syncwarp();
+        mma_commit(&s_full[t * 2 + (j & 1)]);
       }
+      __syncwarp();
     };
     bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag));
     if (ok) {
@@ -191,28 +193,22 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         tc_fence_after();
         issue_s(j1);
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag) &&
+                                       mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)))
+        break;
+      tc_fence_after();
       const uint32_t vb = smem_u32(sKV + st * TA_STAGE + 2 * TA_KCHUNK);
-      for (int t = 0; t < 2; ++t) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + 256 + t * 128;
-        const uint32_t pa = tmem + t * 128 + (j & 1) * 64;
-        if (leader) {
+      const uint32_t d = tmem + 256 + t * 128;
+      const uint32_t pa = tmem + t * 128 + (j & 1) * 64;
+      if (leader) {
 #pragma unroll
-          for (int ks = 0; ks < TA_BK / 16; ++ks) {
-            const uint64_t db = sdesc_mnmajor_sw128(vb + ks * 2048, TA_KCHUNK);
-            mma_f16_ts(d, pa + ks * 8, db, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&pv_done[t]);
+        for (int ks = 0; ks < TA_BK / 16; ++ks) {
+          const uint64_t db = sdesc_mnmajor_sw128(vb + ks * 2048, TA_KCHUNK);
+          mma_f16_ts(d, pa + ks * 8, db, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
         }
-        __syncwarp();
+        mma_commit(&pv_done[t]);
+        mma_commit(&kv_empty[st]);  // this tile's reads of stage st (S_t(j), P_t(j) V_j) issued
       }
-      if (!ok) break;
-      if (leader) mma_commit(&kv_empty[st]);
       __syncwarp();
     }
     if (leader) mma_commit(drain);
