@@ -247,7 +247,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       // row max: four independent partial maxima (no 64-long dependency chain)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < 64; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+      for (int e = 0; e < 64; e += 2)
+        mx4[(e >> 1) & 3] = max3f(mx4[(e >> 1) & 3], __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
       const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
       const bool need = m_tile > m_used + TA_RESCALE_THRESHOLD;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -272,12 +273,14 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       }
       if (need) m_used = m_tile;
       uint32_t pk[32];
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums (two packed pairs)
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sc, -m_used));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sc, -m_used));
-        ls[e & 3] += p0 + p1;
+        float x0, x1;
+        fma2_sc(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]), sc, -m_used, x0, x1);
+        const float p0 = ex2_approx(x0);
+        const float p1 = ex2_approx(x1);
+        add2_acc(ls[2 * (e & 1)], ls[2 * (e & 1) + 1], p0, p1);
         pk[e] = pack_bf16x2(p0, p1);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
