@@ -45,7 +45,7 @@ def _args():
     ap.add_argument("--config", default="minicpm5-1b")
     ap.add_argument("--global-bs", type=int, default=32)
     ap.add_argument("--seq", type=int, default=8192)
-    ap.add_argument("--latency-runs", type=int, default=20)
+    ap.add_argument("--latency-runs", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
@@ -53,6 +53,9 @@ def _args():
                     help="time one isolated kernel of the forward (profiling driver) instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
     ap.add_argument("--kernel-iters", type=int, default=3)
+    ap.add_argument("--isolated", action="store_true",
+                    help="time the isolated-kernel configuration (GEMMs at M=8192, attention at S=8192) and print "
+                         "one JSON line per kernel instead of the bench")
     return ap.parse_args()
 
 
@@ -225,6 +228,58 @@ def run_reference(a, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_isolated(a):
+    """The isolated-kernel configuration: int8 weight-only GEMMs at M=8192 (K=1536, N=1792 QKV /
+    1536 o_proj / 8192 gate+up; K=4096, N=1536 down) with their forward epilogues, and causal GQA
+    attention at S=8192 with 16 Q / 2 KV heads, head_dim 96 and 128, batch 1 and 8.  Inputs and
+    weights ~N(0,1), weights quantised per output channel.  CUDA-event time of each launch (1 warm-up,
+    --kernel-iters timed), with L2 flushed before every timed launch (a 256 MB buffer is rewritten)."""
+    from minicpm5_mk import _lib, ops
+    from minicpm5_mk.mk_weights import quantize_per_out_channel
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    peak = _peaks()[0]["bf16_tflops"]
+
+    flush = torch.empty((64 * 1024 * 1024,), dtype=torch.float32, device=dev)  # 256 MB > L2
+
+    def timeit(fn):
+        fn()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(a.kernel_iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        return total / a.kernel_iters
+
+    M = 8192
+    for name, N, K, mode in (("gemm_qkv", 1792, 1536, _lib.MK_GEMM_ROWSCALE), ("gemm_o_proj", 1536, 1536, _lib.MK_GEMM_RESID32),
+                             ("gemm_gate_up", 8192, 1536, _lib.MK_GEMM_SWIGLU), ("gemm_down", 1536, 4096, _lib.MK_GEMM_RESID32)):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        w8, s = quantize_per_out_channel(torch.randn((N, K), generator=g, device=dev))
+        rstd = torch.ones((M,), device=dev)
+        out = torch.empty((M, N // 2 if mode == _lib.MK_GEMM_SWIGLU else N), dtype=torch.bfloat16, device=dev)
+        x32 = torch.zeros((M, N), dtype=torch.float32, device=dev) if mode == _lib.MK_GEMM_RESID32 else None
+        ms = timeit(lambda: ops.gemm_w8a16(x, w8, s, mode, row_scale=rstd, resid_scale=0.3, out=out, resid32=x32))
+        tf = 2.0 * M * N * K / ms / 1e9
+        print(json.dumps({"kernel": name, "M": M, "N": N, "K": K, "ms": round(ms, 4), "tflops": round(tf, 1),
+                          "frac_of_measured_peak": round(tf / peak, 4)}))
+    for hd in (96, 128):
+        for bs in (1, 8):
+            S, nq, nkv = 8192, 16, 2
+            qkv = torch.randn((bs * S, (nq + 2 * nkv) * hd), generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty((bs * S, nq * hd), dtype=torch.bfloat16, device=dev)
+            ms = timeit(lambda: ops.attention_prefill(qkv, bs, S, nq, nkv, hd, softmax_scale=hd ** -0.5, out=out))
+            tf = 2.0 * S * S * hd * nq * bs / ms / 1e9
+            print(json.dumps({"kernel": "attention", "batch": bs, "seq": S, "heads": f"{nq}q/{nkv}kv", "head_dim": hd,
+                              "ms": round(ms, 4), "tflops": round(tf, 1), "frac_of_measured_peak": round(tf / peak, 4)}))
+
+
 def main():
     a = _args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -235,6 +290,9 @@ def main():
         return
     if a.kernel:
         run_kernel(a)
+        return
+    if a.isolated:
+        run_isolated(a)
         return
     import torch.distributed as dist
     from datetime import timedelta
