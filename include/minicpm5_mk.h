@@ -161,6 +161,14 @@ mk_status mk_rms_rstd(const float* x, int32_t T, int32_t H, int32_t ld, float ep
 mk_status mk_embed(const int32_t* ids, int32_t T, const void* embed, int32_t V, int32_t H, float scale, float* x32,
                    void* xb, void* stream);
 
+/* Top-k log-probabilities of each row of f32 logits [bs, ld] (first V entries):
+ * logprobs[b, r] = logits[b, ids[b, r]] - logsumexp(logits[b, :V]) for the k largest logits in
+ * descending order (equal logits: lower id first).  ids int32 [bs, k], logprobs f32 [bs, k];
+ * 1 <= k <= 64.  Replaces the golden's log_softmax + top-k (benchmark/f32_golden.py:100-102) that the
+ * reference's gate scorer compares (benchmark/gate.py:16-121). */
+mk_status mk_topk_logprobs(const float* logits, int32_t bs, int32_t V, int32_t ld, int32_t k, int32_t* ids,
+                           float* logprobs, void* stream);
+
 /* logits[b] = h[b] @ lm_head^T (f32), top1[b] = argmax (ties -> lowest id) for h f32 [bs, H].
  * part_val/part_idx: scratch of bs * mk_lm_head_parts() entries each.
  * (vLLM LogitsProcessor + greedy sampler after the reference op.) */

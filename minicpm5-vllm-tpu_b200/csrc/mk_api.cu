@@ -629,6 +629,16 @@ mk_status mk_lm_head_argmax(const float* hvec, int32_t bs, int32_t H, const void
                         static_cast<cudaStream_t>(stream));
 }
 
+mk_status mk_topk_logprobs(const float* logits, int32_t bs, int32_t V, int32_t ld, int32_t k, int32_t* ids,
+                           float* logprobs, void* stream) {
+  if (!logits || !ids || !logprobs) return MK_ERR_BAD_ARG;
+  if (bs <= 0 || V <= 0 || ld < V || k <= 0 || k > mk::TOPK_MAX || k > V) return MK_ERR_BAD_SHAPE;
+  if (reinterpret_cast<uintptr_t>(logits) & 3u) return MK_ERR_BAD_ALIGN;
+  mk::topk_logprobs_kernel<<<bs, mk::TOPK_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(logits, V, ld, k, ids,
+                                                                                          logprobs);
+  return cuda_status(cudaGetLastError());
+}
+
 // ------------------------------------------------------------------------------ allocation-free lm_head
 }  // extern "C"
 

@@ -262,4 +262,102 @@ __global__ void argmax_reduce_kernel(const float* __restrict__ part_val, const i
   if (lane == 0) top1[b] = bi;
 }
 
+// ----------------------------------------------------------------------------------------------
+// Top-k log-probabilities of each row of f32 logits [bs, V]: logprob = logit - logsumexp(row), and the
+// k largest in descending order (equal logits: lower id first).  One 1024-thread CTA per row.
+// Reference: the golden's log_softmax + top-k (benchmark/f32_golden.py:100-102), which the gate scorer
+// compares (benchmark/gate.py:16-121); vLLM's logprobs path on the plugin's GPU runner.
+// Selection runs k rounds of a block-wide arg-max restricted to the entries ordered after the previous
+// pick in (value descending, id ascending) order, so no per-thread candidate lists are kept.
+constexpr int TOPK_THREADS = 1024;
+constexpr int TOPK_MAX = 64;
+
+__device__ __forceinline__ bool topk_after(float v, int i, float pv, int pi) {
+  return v < pv || (v == pv && i > pi);  // (v, i) comes after (pv, pi)
+}
+__device__ __forceinline__ bool topk_better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(TOPK_THREADS)
+    topk_logprobs_kernel(const float* __restrict__ logits, int V, int ld, int k, int32_t* __restrict__ ids,
+                         float* __restrict__ lps) {
+  __shared__ float red_v[TOPK_THREADS / 32];
+  __shared__ int red_i[TOPK_THREADS / 32];
+  __shared__ float bcast_v;
+  __shared__ int bcast_i;
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const float* row = logits + static_cast<size_t>(b) * ld;
+  // 1) row max (the first pick) and 2) logsumexp
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < V; i += TOPK_THREADS) {
+    const float v = row[i];
+    if (topk_better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+  auto block_best = [&](float v, int i) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (topk_better(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+    if (lane == 0) { red_v[w] = v; red_i[w] = i; }
+    __syncthreads();
+    if (w == 0) {
+      v = red_v[lane];
+      i = red_i[lane];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (topk_better(ov, oi, v, i)) { v = ov; i = oi; }
+      }
+      if (lane == 0) { bcast_v = v; bcast_i = i; }
+    }
+    __syncthreads();
+  };
+  block_best(bv, bi);
+  const float m = bcast_v;
+  float se = 0.f;
+  for (int i = tid; i < V; i += TOPK_THREADS) se += __expf(row[i] - m);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+  __syncthreads();
+  if (lane == 0) red_v[w] = se;
+  __syncthreads();
+  if (w == 0) {
+    float t = red_v[lane];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red_v[0] = t;
+  }
+  __syncthreads();
+  const float lse = m + logf(red_v[0]);
+  __syncthreads();
+  // 3) k picks
+  float pv = bcast_v;
+  int pi = bcast_i;
+  if (tid == 0) {
+    ids[static_cast<size_t>(b) * k] = pi;
+    lps[static_cast<size_t>(b) * k] = pv - lse;
+  }
+  for (int r = 1; r < k; ++r) {
+    bv = -INFINITY;
+    bi = 0x7fffffff;
+    for (int i = tid; i < V; i += TOPK_THREADS) {
+      const float v = row[i];
+      if (topk_after(v, i, pv, pi) && topk_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    block_best(bv, bi);
+    pv = bcast_v;
+    pi = bcast_i;
+    if (tid == 0) {
+      ids[static_cast<size_t>(b) * k + r] = pi;
+      lps[static_cast<size_t>(b) * k + r] = pv - lse;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace mk

@@ -16,6 +16,7 @@ EXPORTED = (
     "mk_status_string", "mk_version", "mk_create", "mk_bind_weights", "mk_workspace_size", "mk_forward",
     "mk_get_error", "mk_destroy", "mk_gemm_w8a16", "mk_attention_prefill", "mk_rope", "mk_rms_rstd", "mk_embed",
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward", "mk_lm_head_argmax_noalloc",
+    "mk_topk_logprobs",
 )
 
 MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
@@ -72,6 +73,7 @@ def lib() -> ctypes.CDLL:
         L.mk_lm_head_parts.argtypes = []
         L.mk_lm_head_argmax.argtypes = [_vp, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp]
         L.mk_lm_head_argmax_noalloc.argtypes = [_vp, _i32, _i32, _vp, _i32, _vp, _vp, _vp]
+        L.mk_topk_logprobs.argtypes = [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]
         L.mk_launches_per_forward.restype = _i32
         L.mk_launches_per_forward.argtypes = [_vp, _i32, _i32]
         for name in EXPORTED:

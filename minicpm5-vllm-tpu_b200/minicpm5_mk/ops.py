@@ -199,3 +199,19 @@ def lm_head_argmax(h: torch.Tensor, w: torch.Tensor):
                                       pi.data_ptr(), top1.data_ptr(), _stream(h.device))
     _lib.check(st, "mk_lm_head_argmax")
     return logits, top1
+
+
+def topk_logprobs(logits: torch.Tensor, k: int = 20):
+    """Top-k log-probabilities of each row of f32 logits [bs, V] on the GPU (mk_topk_logprobs):
+    (ids int32 [bs, k], logprobs f32 [bs, k]), descending, equal logits -> lower id first.
+    The golden's log_softmax + top-k (benchmark/f32_golden.py:100-102)."""
+    _cuda(logits, "logits")
+    if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a row-major f32 [bs, V] tensor")
+    bs, V = logits.shape
+    ids = torch.empty((bs, k), dtype=torch.int32, device=logits.device)
+    lps = torch.empty((bs, k), dtype=torch.float32, device=logits.device)
+    st = _lib.lib().mk_topk_logprobs(logits.data_ptr(), bs, V, logits.stride(0), k, ids.data_ptr(), lps.data_ptr(),
+                                     _stream(logits.device))
+    _lib.check(st, "mk_topk_logprobs")
+    return ids, lps

@@ -103,19 +103,24 @@ def make_gate(ref_root):
     gate = _load(os.path.join(ref_root, "benchmark", "gate.py"), "ref_gate")
     rng = np.random.default_rng(5)
     cases = []
-    for c in range(4):
+    # noise levels 0.02..0.08 (PASS), 0.17 (JUDGE), then 0.25 and 1.0 (FAIL); the last two cases
+    # also carry a no-logprobs sampled token
+    for c, noise_scale in enumerate((0.02, 0.04, 0.06, 0.08, 0.17, 0.25, 1.0)):
         ref_sets, cand_sets = [], []
         for bs in (1, 2):
             rs, cs = [], []
             for _ in range(bs):
                 logits = rng.normal(size=200) * (1.0 + c)
-                noise = rng.normal(size=200) * (0.02 * (c + 1))
+                noise = rng.normal(size=200) * noise_scale
                 lr = logits - np.log(np.exp(logits).sum())
                 lc = (logits + noise) - np.log(np.exp(logits + noise).sum())
                 ir = np.argsort(-lr)[:20]
                 ic = np.argsort(-lc)[:20]
                 rs.append({"top_ids": ir.tolist(), "top_logprobs": lr[ir].tolist()})
-                cs.append({"top_ids": ic.tolist(), "top_logprobs": lc[ic].tolist()})
+                cand = {"top_ids": ic.tolist(), "top_logprobs": lc[ic].tolist()}
+                if c >= 5:
+                    cand["sampled_nolp"] = int(ic[0] if rng.random() < 0.5 else ic[1])
+                cs.append(cand)
             ref_sets.append({"batch_size": bs, "seq_len": 64, "seqs": rs})
             cand_sets.append({"batch_size": bs, "seq_len": 64, "seqs": cs})
         cases.append({"ref": ref_sets, "cand": cand_sets, "report": gate.compare_gate(ref_sets, cand_sets)})

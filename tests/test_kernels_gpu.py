@@ -233,3 +233,21 @@ def test_lm_head_argmax(dev, bs, H, V):
     assert torch.equal(top1.cpu().long(), torch.argmax(lg, dim=-1))
     if V > 100:
         assert int(top1[0]) == 17
+
+
+@pytest.mark.parametrize("bs,V,k", [(3, 73448, 20), (2, 1000, 64), (1, 130560, 1)])
+def test_topk_logprobs(dev, bs, V, k):
+    from minicpm5_mk import ops
+    from oracle import golden
+    lg = torch.randn((bs, V), generator=_gen(61)) * 3.0
+    lg[0, 11] = lg[0, 5] = lg[0].max() + 1.0  # planted tie at the top: lower id first
+    ids, lps = ops.topk_logprobs(lg.to(dev), k)
+    torch.cuda.synchronize()
+    ids, lps = ids.cpu(), lps.cpu()
+    for b in range(bs):
+        ref_ids, ref_lps = golden.topk_logprobs(lg[b], k)
+        if b == 0:  # torch.topk leaves the order of equal values open
+            assert ids[0, 0].item() == 5 and (k == 1 or ids[0, 1].item() == 11)
+            ref_ids = [5, 11][:k] + ref_ids[2:] if k > 1 else [5]
+        assert ids[b].tolist() == ref_ids, b
+        assert max(abs(a - r) for a, r in zip(lps[b].tolist(), ref_lps)) < 2e-5

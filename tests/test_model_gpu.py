@@ -109,3 +109,26 @@ def test_forward_1b_s8192_vs_committed_golden(golden_dir):
     assert cos >= COS_MIN, cos
     assert (ref - got).abs().max().item() <= MAXABS_FRAC * fx["logit_range"]
     assert abs((lg.max() - lg.min()).item() - fx["logit_range"]) <= MAXABS_FRAC * fx["logit_range"]
+
+
+@pytest.mark.parametrize("name", ["tiny96_s256", "tiny128_s384"])
+def test_forward_topk_passes_reference_gate(golden_dir, name):
+    """GPU forward + GPU top-20 log-probs scored against the reference's own forward_one top-20 dump
+    with the reference's gate (restated in oracle/gate.py, pinned on its reports): gate v2 PASS and
+    top-1 agreement 1.0."""
+    from minicpm5_mk import ops
+    from oracle.gate import compare_gate
+    fx = json.load(open(os.path.join(golden_dir, f"golden_f32_{name}.json")))
+    cfg = PRESETS[fx["preset"]].replace(**fx["overrides"])
+    eng, _ = _engine(cfg, random_state_dict(cfg, seed=fx["seed"]))
+    ids = torch.tensor(fx["prompt_token_ids"], dtype=torch.int32)
+    bs, S = ids.shape
+    _, lg, top1 = eng.forward(ids.reshape(-1).contiguous().cuda(), bs, S)
+    tid, tlp = ops.topk_logprobs(lg, 20)
+    torch.cuda.synchronize()
+    cand = [{"top_ids": tid[b].tolist(), "top_logprobs": tlp[b].tolist()} for b in range(bs)]
+    ref = [{"batch_size": bs, "seq_len": S, "seqs": fx["seqs"]}]
+    rep = compare_gate(ref, [{"batch_size": bs, "seq_len": S, "seqs": cand}])
+    assert rep["gate_v2"] == "PASS", rep
+    assert rep["top1_agreement"] == 1.0
+    assert all(int(top1[b]) == cand[b]["top_ids"][0] for b in range(bs))

@@ -103,3 +103,15 @@ def test_design_meets_accuracy_bar_1b_s1024():
     assert cos >= 0.999
     assert (lg_g - lg_m[0]).abs().max().item() <= 2e-2 * rng
     assert golden.argmax_first(lg_g) == golden.argmax_first(lg_m[0])
+
+
+def test_gate_scorer_matches_reference_reports(golden_dir):
+    """oracle/gate.py against the reference's own compare_gate reports (PASS, JUDGE and FAIL verdicts,
+    with and without a no-logprobs sampled token): every field identical."""
+    from oracle.gate import compare_gate
+    cases = json.load(open(os.path.join(golden_dir, "gate_cases.json")))
+    verdicts = set()
+    for c in cases:
+        assert compare_gate(c["ref"], c["cand"]) == c["report"]
+        verdicts.add(c["report"]["gate_v2"])
+    assert verdicts == {"PASS", "JUDGE", "FAIL"}
