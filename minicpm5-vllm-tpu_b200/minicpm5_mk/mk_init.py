@@ -75,11 +75,13 @@ def random_state_dict(cfg: MkConfig, seed: int = 1234, std: float = 0.02,
 def synthetic_ids(bs: int, seq: int, seed: int = 1234, lo: int = 1000, hi: int = 30000,
                   vocab: int | None = None) -> "torch.Tensor":
     """(bs, seq) int32 token ids uniform in [lo, min(hi, vocab)), numpy default_rng(seed)
-    (the reference draws prompt ids from [1000, min(vocab, 30000)), `benchmark/run_benchmark.py:341-348`)."""
+    (the reference draws prompt ids from [1000, min(vocab, 30000)), `benchmark/run_benchmark.py:341-348`).
+    Vocabularies no larger than lo (the tiny test models) draw from the whole [0, vocab)."""
     import numpy as np
 
     if vocab is not None:
         hi = min(hi, vocab)
-        lo = min(lo, max(0, hi - 1))
+        if lo >= hi:
+            lo = 0
     rng = np.random.default_rng(seed)
     return torch.from_numpy(rng.integers(lo, hi, size=(bs, seq), dtype=np.int64).astype(np.int32))

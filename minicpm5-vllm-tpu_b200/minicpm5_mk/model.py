@@ -170,6 +170,12 @@ class MiniCPM5MegakernelForCausalLM(LlamaForCausalLM):
                 hid, _, _ = self._mk_engine.forward(ids, bs, seq, logits=False)
                 return scatter_last(hid, bs, seq, int(input_ids.shape[0]))
         self._mk_counts["stock"] += 1
+        st = getattr(self, "_mk_status", None)
+        if st is not None:  # why steps take the stock path (written when a new reason first appears)
+            reasons = st.setdefault("stock_reasons", {})
+            reasons[reason] = reasons.get(reason, 0) + 1
+            if reasons[reason] == 1:
+                self._mk_write_status()
         if getattr(self, "_mk_stock_freed", False):
             if reason == "dummy":
                 return torch.zeros((input_ids.shape[0], self._mk_cfg.hidden), dtype=torch.bfloat16,
