@@ -110,6 +110,32 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
 /* Number of kernel launches one mk_forward(bs, seq) issues (for launch accounting). */
 int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq);
 
+/* Per-stage device time of one forward, measured with CUDA events recorded on `stream` between
+ * the launches (the interval after a launch runs up to the next launch's start, so gaps are
+ * charged to the stage before them).  Index by mk_stage. */
+typedef enum mk_stage {
+  MK_STAGE_EMBED = 0,      /* embedding gather (+ row sums of squares) */
+  MK_STAGE_QKV = 1,        /* QKV projection with RMSNorm and RoPE, layers 0..L-2 */
+  MK_STAGE_ATTN = 2,       /* causal prefill attention, layers 0..L-2 */
+  MK_STAGE_O = 3,          /* o_proj with the residual update */
+  MK_STAGE_GATE_UP = 4,    /* gate/up projection with SiLU * up */
+  MK_STAGE_DOWN = 5,       /* down projection with the residual update */
+  MK_STAGE_LAST_LAYER = 6, /* the last layer (K/V for every position, the rest for the last one) */
+  MK_STAGE_HEAD = 7,       /* final norm, lm_head and argmax */
+  MK_STAGES = 8
+} mk_stage;
+
+typedef struct mk_stage_times {
+  float ms[MK_STAGES];         /* summed device milliseconds per stage */
+  int32_t launches[MK_STAGES]; /* kernel launches per stage */
+} mk_stage_times;
+
+/* mk_forward with per-stage timing: the same launches on the same stream, with CUDA events
+ * between them.  Synchronises the stream before returning and fills *times. */
+mk_status mk_forward_timed(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                           size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream,
+                           mk_stage_times* times);
+
 /* Read and clear the library's device error word (synchronises the device).  *device_err
  * receives the raw code (0 = none); the return value maps it to an mk_status. */
 mk_status mk_get_error(mk_handle* h, int32_t* device_err);

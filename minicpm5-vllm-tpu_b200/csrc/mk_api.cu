@@ -401,8 +401,54 @@ mk_status mk_workspace_size(const mk_handle* h, int32_t bs, int32_t seq, size_t*
   return MK_OK;
 }
 
-mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
-                     size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream) {
+}  // extern "C"
+
+namespace {
+// Per-stage timing of one forward: an event before the first launch and one after each stage's
+// launches, all on the forward's stream.  A null clock records nothing.
+class StageClock {
+ public:
+  ~StageClock() {
+    for (cudaEvent_t e : ev_) cudaEventDestroy(e);
+  }
+  mk_status start(cudaStream_t st) {
+    st_ = st;
+    return record();
+  }
+  mk_status mark(int stage, int launches) {
+    stage_.push_back(stage);
+    launches_.push_back(launches);
+    return record();
+  }
+  mk_status finish(mk_stage_times* out) {
+    std::memset(out, 0, sizeof(*out));
+    if (ev_.empty()) return MK_OK;
+    MK_CUDA(cudaEventSynchronize(ev_.back()));
+    for (size_t i = 0; i < stage_.size(); ++i) {
+      float ms = 0.f;
+      MK_CUDA(cudaEventElapsedTime(&ms, ev_[i], ev_[i + 1]));
+      out->ms[stage_[i]] += ms;
+      out->launches[stage_[i]] += launches_[i];
+    }
+    return MK_OK;
+  }
+
+ private:
+  mk_status record() {
+    cudaEvent_t e;
+    MK_CUDA(cudaEventCreate(&e));
+    ev_.push_back(e);
+    MK_CUDA(cudaEventRecord(e, st_));
+    return MK_OK;
+  }
+  cudaStream_t st_ = nullptr;
+  std::vector<cudaEvent_t> ev_;
+  std::vector<int> stage_, launches_;
+};
+
+mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                       size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream,
+                       StageClock* clk) {
   if (!h || !d_ids || !d_workspace) return MK_ERR_BAD_ARG;
   if (!h->bound) return MK_ERR_NOT_BOUND;
   const mk_config& c = h->cfg;
@@ -440,9 +486,12 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
   const int np = H / 128;       // 128-column tiles of the residual: RMSNorm partial sums per row
+  auto mark = [&](int stage, int launches) { return clk ? clk->mark(stage, launches) : MK_OK; };
+  if (clk) MK_TRY(clk->start(st));
   mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
       d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err, rowsq, np);
   MK_CUDA(cudaGetLastError());
+  MK_TRY(mark(MK_STAGE_EMBED, 1));
 
   // RMSNorm folded into the projections: rstd comes from the residual's per-tile sums of squares
   // (written by the embedding and by every residual-update epilogue).
@@ -475,13 +524,18 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
     MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
                        h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st, nullptr, 0,
                        with_rope(norm_from(rowsq), qd + kvd, seq, 0)));
+    MK_TRY(mark(MK_STAGE_QKV, 1));
     MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
+    MK_TRY(mark(MK_STAGE_ATTN, 1));
     MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+    MK_TRY(mark(MK_STAGE_O, 1));
     MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0, norm_from(rowsq)));
+    MK_TRY(mark(MK_STAGE_GATE_UP, 1));
     MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+    MK_TRY(mark(MK_STAGE_DOWN, 1));
   }
 
   // Last layer: K/V for every position, everything else for the last position only
@@ -517,13 +571,32 @@ mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
+    MK_TRY(mark(MK_STAGE_LAST_LAYER, 7));
   }
 
   mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
                                             c.eps, c.logit_scale);
   MK_CUDA(cudaGetLastError());
-  return lm_head_launch(d, hf, bs, H, h->w.lm_head, c.vocab, logits, f32(ws.pval),
-                        reinterpret_cast<int*>(base + ws.pidx), top1, st);
+  MK_TRY(lm_head_launch(d, hf, bs, H, h->w.lm_head, c.vocab, logits, f32(ws.pval),
+                        reinterpret_cast<int*>(base + ws.pidx), top1, st));
+  return mark(MK_STAGE_HEAD, 1 + (bs + mk::LM_ROWS - 1) / mk::LM_ROWS + 1);
+}
+}  // namespace
+
+extern "C" {
+
+mk_status mk_forward(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                     size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream) {
+  return forward_impl(h, d_ids, bs, seq, d_workspace, workspace_bytes, d_hidden, d_logits, d_top1, stream, nullptr);
+}
+
+mk_status mk_forward_timed(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
+                           size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream,
+                           mk_stage_times* times) {
+  if (!times) return MK_ERR_BAD_ARG;
+  StageClock clk;
+  MK_TRY(forward_impl(h, d_ids, bs, seq, d_workspace, workspace_bytes, d_hidden, d_logits, d_top1, stream, &clk));
+  return clk.finish(times);
 }
 
 int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq) {

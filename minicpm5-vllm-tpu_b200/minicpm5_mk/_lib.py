@@ -16,7 +16,7 @@ EXPORTED = (
     "mk_status_string", "mk_version", "mk_create", "mk_bind_weights", "mk_workspace_size", "mk_forward",
     "mk_get_error", "mk_destroy", "mk_gemm_w8a16", "mk_attention_prefill", "mk_rope", "mk_rms_rstd", "mk_embed",
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward", "mk_lm_head_argmax_noalloc",
-    "mk_topk_logprobs",
+    "mk_topk_logprobs", "mk_forward_timed",
 )
 
 MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
@@ -33,6 +33,13 @@ class MkConfigC(ctypes.Structure):
 class MkWeightPtrsC(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("embed", "lm_head", "final_norm", "rope_cos", "rope_sin", "w_qkv", "s_qkv",
                                    "w_o", "s_o", "w_gu", "s_gu", "w_down", "s_down")]
+
+
+MK_STAGE_NAMES = ("embed", "qkv", "attn", "o_proj", "gate_up", "down", "last_layer", "head")
+
+
+class MkStageTimesC(ctypes.Structure):
+    _fields_ = [("ms", _f32 * len(MK_STAGE_NAMES)), ("launches", _i32 * len(MK_STAGE_NAMES))]
 
 
 class MkError(RuntimeError):
@@ -59,6 +66,8 @@ def lib() -> ctypes.CDLL:
         L.mk_bind_weights.argtypes = [_vp, ctypes.POINTER(MkWeightPtrsC)]
         L.mk_workspace_size.argtypes = [_vp, _i32, _i32, ctypes.POINTER(_sz)]
         L.mk_forward.argtypes = [_vp, _vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _vp]
+        L.mk_forward_timed.argtypes = [_vp, _vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _vp,
+                                       ctypes.POINTER(MkStageTimesC)]
         L.mk_get_error.argtypes = [_vp, ctypes.POINTER(_i32)]
         L.mk_destroy.restype = None
         L.mk_destroy.argtypes = [_vp]

@@ -78,7 +78,11 @@ class MkEngine:
         return self._ws
 
     def forward(self, ids: torch.Tensor, bs: int, seq: int, *, hidden: bool = True, logits: bool = True,
-                out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+                out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+                stage_times: Optional[dict] = None):
+        """Prefill-score forward through `mk_forward`.  With a `stage_times` dict, the same launches run
+        through `mk_forward_timed` (CUDA events between them, stream synchronised on return) and the dict
+        receives {stage: {"ms": device ms, "launches": n}}."""
         _cuda(ids, "ids")
         if ids.dtype != torch.int32:
             raise ValueError("minicpm5_mk: ids must be int32")
@@ -91,9 +95,18 @@ class MkEngine:
             hid = torch.empty((bs, self.cfg.hidden), dtype=torch.bfloat16, device=self.device) if hidden else None
             lg = torch.empty((bs, self.cfg.vocab), dtype=torch.float32, device=self.device) if logits else None
             top1 = torch.empty((bs,), dtype=torch.int32, device=self.device)
-        st = _lib.lib().mk_forward(self._h, ids.data_ptr(), bs, seq, ws.data_ptr(), ws.numel(), _ptr(hid), _ptr(lg),
-                                   top1.data_ptr(), _stream(self.device))
-        _lib.check(st, "mk_forward")
+        if stage_times is None:
+            st = _lib.lib().mk_forward(self._h, ids.data_ptr(), bs, seq, ws.data_ptr(), ws.numel(), _ptr(hid),
+                                       _ptr(lg), top1.data_ptr(), _stream(self.device))
+            _lib.check(st, "mk_forward")
+        else:
+            t = _lib.MkStageTimesC()
+            st = _lib.lib().mk_forward_timed(self._h, ids.data_ptr(), bs, seq, ws.data_ptr(), ws.numel(), _ptr(hid),
+                                             _ptr(lg), top1.data_ptr(), _stream(self.device), ctypes.byref(t))
+            _lib.check(st, "mk_forward_timed")
+            stage_times.clear()
+            for i, name in enumerate(_lib.MK_STAGE_NAMES):
+                stage_times[name] = {"ms": float(t.ms[i]), "launches": int(t.launches[i])}
         return hid, lg, top1
 
     def launches_per_forward(self, bs: int, seq: int) -> int:

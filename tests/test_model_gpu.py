@@ -72,6 +72,26 @@ def test_forward_batch_invariance():
     assert int(t4[2]) == int(t1[0])
 
 
+def test_forward_timed_matches_forward():
+    """mk_forward_timed runs the same launches as mk_forward (bit-identical outputs), counts every launch
+    once and charges positive device time to each stage."""
+    cfg = PRESETS["tiny-hd96"]
+    eng, _ = _engine(cfg, random_state_dict(cfg, seed=1234))
+    bs, S = 2, 256
+    ids = synthetic_ids(bs, S, seed=11, vocab=cfg.vocab).reshape(-1).contiguous().cuda()
+    h0, l0, t0 = eng.forward(ids, bs, S)
+    stages = {}
+    h1, l1, t1 = eng.forward(ids, bs, S, stage_times=stages)
+    torch.cuda.synchronize()
+    assert torch.equal(h0, h1) and torch.equal(l0, l1) and torch.equal(t0, t1)
+    assert sum(v["launches"] for v in stages.values()) == eng.launches_per_forward(bs, S)
+    L = cfg.num_layers
+    for name in ("qkv", "attn", "o_proj", "gate_up", "down"):
+        assert stages[name]["launches"] == L - 1, (name, stages[name])
+    assert stages["last_layer"]["launches"] == 7
+    assert all(v["ms"] > 0 for v in stages.values()), stages
+
+
 def test_forward_1b_s1024_vs_golden():
     from oracle import golden
     cfg = PRESETS["minicpm5-1b"]
