@@ -25,7 +25,8 @@
 //               rare; P stays <= 256.  At the end the same threads normalise O_t by the row sum and
 //               store bf16 rows.
 //
-// TMEM (512 columns): S_t[b] at [128t + 64b, +64) for tile t and buffer b; O_t at [256 + 128t, +hd).
+// TMEM (512 columns): S_t[b] at [128t + 64b, +64) for tile t and buffer b; O_t at [256 + 128t, +hd);
+// for head_dim 96, Q_t's dimensions [0, 64) as bf16 pairs at [256 + 128t + 96, +32).
 // Shared memory: Q 2 tiles x 2 chunks (128 rows x 128 B each), K and V 4 stages x 2 chunks
 // (64 rows x 128 B each).  head_dim 96 uses a second 64-column chunk whose upper 32 columns are
 // TMA zero-fill and never read by the MMAs.
@@ -43,6 +44,30 @@ constexpr uint32_t TA_KCHUNK = TA_BK * 128;  // 64 rows x 128 bytes
 constexpr uint32_t TA_STAGE = 4 * TA_KCHUNK;  // K (2 chunks) + V (2 chunks)
 constexpr size_t TA_SMEM = 1024 + 4 * TA_QCHUNK + TA_STAGES * TA_STAGE + 256;
 constexpr float TA_RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+// head_dim 96 leaves 32 TMEM columns after each O_t: they hold Q_t's first 64 dimensions, so the first
+// four K-steps of S = Q K^T take A from TMEM and read only K from shared memory.  An SS UMMA with
+// N = 64 is bound by shared-memory bandwidth (6 KB of operands per 32 tensor cycles); from TMEM it
+// runs at the full tensor rate.
+template <int HD>
+__host__ __device__ constexpr int ta_q_tmem_ksteps() { return HD == 96 ? 4 : 0; }
+
+// Pairs of softmax exponentials e with (e & TA_FMA_EXP_MASK) == TA_FMA_EXP_MASK go to the FMA pipe.
+constexpr int TA_FMA_EXP_MASK = 7;
+
+// 2^x on the FMA pipe for a share of the softmax exponentials: 16 MUFU results per clock per SM
+// cannot keep up with the tensor core at head_dim 96.  x = j + f with j = round(x) (adding
+// 1.5 * 2^23 rounds x into the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f is a cubic fitted by
+// least squares to 2^f on [-0.5, 0.5] (max relative error 7.8e-5, far below the bf16 rounding of P);
+// 2^j is added to the exponent field.  x is clamped at -125 (result about 2e-38, so the exponent
+// field stays positive; -inf maps there too).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.0550887659f, f, 0.242604658f), f, 0.693276286f), f, 0.999928892f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
 
 struct AttnTcArgs {
   int S;       // sequence length
@@ -72,7 +97,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   uint64_t* p_ready = s_full + 4;               // [2 tiles][2 buffers]
   uint64_t* pv_done = p_ready + 4;              // [2 tiles]
   uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* q_tm = drain + 1;                   // [2 tiles]: Q_t's first dimensions are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_tm + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,6 +124,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
     mbar_init(drain, 2);
+    mbar_init(&q_tm[0], 4);
+    mbar_init(&q_tm[1], 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -168,15 +196,24 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const int c = ks >> 2;
-          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_QCHUNK)) + 2 * (ks & 3);
           const uint64_t db = sdesc_kmajor_sw128(smem_u32(kb + c * TA_KCHUNK)) + 2 * (ks & 3);
-          mma_f16_ss(d, da, db, idesc_s, ks > 0 ? 1u : 0u);
+          if (ks < ta_q_tmem_ksteps<HD>()) {
+            mma_f16_ts(d, tmem + 256 + t * 128 + HD + ks * 8, db, idesc_s, ks > 0 ? 1u : 0u);
+          } else {
+            const uint64_t da = sdesc_kmajor_sw128(smem_u32(sQ + (t * 2 + c) * TA_QCHUNK)) + 2 * (ks & 3);
+            mma_f16_ss(d, da, db, idesc_s, ks > 0 ? 1u : 0u);
+          }
         }
         mma_commit(&s_full[t * 2 + (j & 1)]);
       }
       __syncwarp();
     };
-    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag));
+    // The path from the softmax's p_ready(j) to S_t(j+2) being ready bounds the loop: O_t += P_t(j) V_j
+    // and S_t(j+2) are issued back to back with no barrier wait between them.  The K/V waits for later
+    // tiles are taken while this warp waits for the softmax anyway.
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag) &&
+                                          (ntiles < 2 || mbar_wait(&k_full[1 % TA_STAGES], 0, abort_flag)) &&
+                                          (ta_q_tmem_ksteps<HD>() == 0 || mbar_wait(&q_tm[t], 0, abort_flag)));
     if (ok) {
       tc_fence_after();
       issue_s(0);
@@ -184,17 +221,19 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     for (int j = 0; ok && j < ntiles; ++j) {
       const int st = j % TA_STAGES;
       if (j + 1 < ntiles) {
-        const int j1 = j + 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[j1 % TA_STAGES], (j1 / TA_STAGES) & 1, abort_flag))) break;
-        // S buffer (j+1)&1 still holds P_t(j-1), read by O_t += P_t(j-1) V.  tcgen05.mma ops issued
-        // by this thread execute in issue order, so S_t(j+1) (issued after that P V) overwrites P_t(j-1)
-        // only after it has been read: no wait, the tensor pipe stays full.  The softmax finished
-        // reading S_t(j-1) before it signalled p_ready for tile j-1, which this thread consumed.
+        // K_{j+1} has landed (waited for in the previous iteration).  S buffer (j+1)&1 still holds
+        // P_t(j-1), read by O_t += P_t(j-1) V.  tcgen05.mma ops issued by this thread execute in issue
+        // order, so S_t(j+1) (issued after that P V) overwrites P_t(j-1) only after it has been read:
+        // no wait, the tensor pipe stays full.  The softmax finished reading S_t(j-1) before it
+        // signalled p_ready for tile j-1, which this thread consumed.
         tc_fence_after();
-        issue_s(j1);
+        issue_s(j + 1);
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag) &&
-                                       mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)))
+      const int j2 = j + 2;
+      if (!__all_sync(0xffffffffu,
+                      (j2 >= ntiles || mbar_wait(&k_full[j2 % TA_STAGES], (j2 / TA_STAGES) & 1, abort_flag)) &&
+                          mbar_wait(&v_full[st], (j / TA_STAGES) & 1, abort_flag) &&
+                          mbar_wait(&p_ready[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)))
         break;
       tc_fence_after();
       const uint32_t vb = smem_u32(sKV + st * TA_STAGE + 2 * TA_KCHUNK);
@@ -227,7 +266,30 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     const float sc = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
+    if constexpr (ta_q_tmem_ksteps<HD>() > 0) {
+      // Q_t row `row`, dimensions [0, 64): the first 128-byte chunk of the row in shared memory (128B
+      // swizzle: 16-byte unit u of row r sits at unit u ^ (r & 7)), copied as bf16 pairs into the
+      // columns after O_t, the layout of a TMEM A operand.
+      ok = mbar_wait(q_full, 0, abort_flag);
+      if (ok) {
+        const uint8_t* qrow = sQ + t * 2 * TA_QCHUNK + row * 128;
+        uint32_t qv[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 w = *reinterpret_cast<const uint4*>(qrow + ((u ^ (row & 7)) << 4));
+          qv[4 * u] = w.x;
+          qv[4 * u + 1] = w.y;
+          qv[4 * u + 2] = w.z;
+          qv[4 * u + 3] = w.w;
+        }
+        tmem_st_32x32b_x32(tO + HD, qv);
+        tmem_st_wait();
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_tm[t]);
+    }
+    for (int j = 0; ok && j < ntiles; ++j) {
       const int b = j & 1;
       if (!mbar_wait(&s_full[t * 2 + b], (j >> 1) & 1, abort_flag)) {
         ok = false;
@@ -278,8 +340,10 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       for (int e = 0; e < 32; ++e) {
         float x0, x1;
         fma2_sc(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]), sc, -m_used, x0, x1);
-        const float p0 = ex2_approx(x0);
-        const float p1 = ex2_approx(x1);
+        // an eighth of the exponentials on the FMA pipe, the rest on MUFU
+        const bool fma_exp = HD == 96 && (e & TA_FMA_EXP_MASK) == TA_FMA_EXP_MASK;
+        const float p0 = fma_exp ? exp2_fma(x0) : ex2_approx(x0);
+        const float p1 = fma_exp ? exp2_fma(x1) : ex2_approx(x1);
         add2_acc(ls[2 * (e & 1)], ls[2 * (e & 1) + 1], p0, p1);
         pk[e] = pack_bf16x2(p0, p1);
       }
