@@ -122,7 +122,8 @@ typedef enum mk_stage {
   MK_STAGE_DOWN = 5,       /* down projection with the residual update */
   MK_STAGE_LAST_LAYER = 6, /* the last layer (K/V for every position, the rest for the last one) */
   MK_STAGE_HEAD = 7,       /* final norm, lm_head and argmax */
-  MK_STAGES = 8
+  MK_STAGE_KV_GATHER = 8,  /* sequence parallel: K/V packing and the caller's all-gather, every layer */
+  MK_STAGES = 9
 } mk_stage;
 
 typedef struct mk_stage_times {
@@ -135,6 +136,38 @@ typedef struct mk_stage_times {
 mk_status mk_forward_timed(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t seq, void* d_workspace,
                            size_t workspace_bytes, void* d_hidden, float* d_logits, int32_t* d_top1, void* stream,
                            mk_stage_times* times);
+
+/* ---------------------------------------------------------------- sequence parallelism
+ * One sequence over `world` GPUs, one rank (process) per GPU (counterpart of `core_forward_sp`,
+ * plugin/minicpm5_mk/mk_jax.py:440-489, generalised from 2 TensorCores to `world` GPUs).  The
+ * sequence is cut into zig-zag blocks: in every group of 2 * world blocks, rank r owns block r and
+ * block 2 * world - 1 - r (`sp_global_block`, plugin/minicpm5_mk/mk_attn.py:721-724).  Each rank runs
+ * the projections and MLPs on its own rows and attention for its own queries.  Once per layer the
+ * ranks all-gather their K/V rows (rank by rank) through the caller's collective.
+ *
+ * The all-gather callback is issued on `stream`, in the same order on every rank: it gathers
+ * `bytes_per_rank` bytes from `d_send` of every rank into `d_recv` (rank r's bytes at offset
+ * r * bytes_per_rank), ordered after the work already on the stream and before the work issued
+ * after it returns (an NCCL all-gather on that stream does this).  It returns 0 on success. */
+typedef int32_t (*mk_allgather_fn)(void* ctx, const void* d_send, void* d_recv, size_t bytes_per_rank, void* stream);
+
+/* Zig-zag block length in tokens for (seq, world), 0 if the shape cannot be split: the largest of
+ * 512, 256, 128, 64 with seq % (2 * world * blk) == 0 that holds whole attention query blocks. */
+int32_t mk_sp_block(const mk_handle* h, int32_t seq, int32_t world);
+
+/* Bytes of workspace mk_forward_sp needs on each rank. */
+mk_status mk_workspace_size_sp(const mk_handle* h, int32_t seq, int32_t world, size_t* bytes);
+
+/* Sequence-parallel prefill-score forward of one sequence of `seq` tokens.
+ *   d_ids   int32 [seq], the whole sequence, on every rank
+ *   d_hidden / d_logits / d_top1 as in mk_forward (bs = 1); written on rank 0 only, which owns the
+ *           last position
+ *   times   optional per-stage device times (as mk_forward_timed; synchronises the stream)
+ * Returns MK_ERR_BAD_ARG for a bad rank / world or a null callback, MK_ERR_BAD_SHAPE when
+ * mk_sp_block is 0, MK_ERR_CUDA when the callback fails. */
+mk_status mk_forward_sp(mk_handle* h, const int32_t* d_ids, int32_t seq, int32_t rank, int32_t world,
+                        mk_allgather_fn allgather, void* allgather_ctx, void* d_workspace, size_t workspace_bytes,
+                        void* d_hidden, float* d_logits, int32_t* d_top1, void* stream, mk_stage_times* times);
 
 /* Read and clear the library's device error word (synchronises the device).  *device_err
  * receives the raw code (0 = none); the return value maps it to an mk_status. */

@@ -127,6 +127,7 @@ struct GemmFusion {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   int rope_cols = 0, head_dim = 0, rope_seq = 1, rope_pos_base = 0;
+  mk::SpLayout sp;  // sequence-parallel rows (RoPE positions)
 };
 
 mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
@@ -157,6 +158,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.head_dim = fu.head_dim > 0 ? fu.head_dim : 1;
   ga.rope_seq = fu.rope_seq > 0 ? fu.rope_seq : 1;
   ga.rope_pos_base = fu.rope_pos_base;
+  ga.sp = fu.sp;
   ga.err = d->err;
   const int tiles = ((M + ga.nt - 1) / ga.nt) * (N / mk::GW);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
@@ -209,22 +211,28 @@ int ilog2(int v) {
   return r;
 }
 
-// tcgen05 causal GQA attention (mk_attn_tc.cuh).
-mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
-                      int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
+// tcgen05 causal GQA attention (mk_attn_tc.cuh).  Queries (rows per sequence `rows`) and keys /
+// values (S per sequence) may live in different buffers; under sequence parallelism the queries are
+// a rank's zig-zag rows and K/V the rank-by-rank all-gather (`sp`).
+mk_status launch_attn_split(const DeviceState* d, const void* q_base, int rows, int ld_q, int q_col, const void* kv_base,
+                            int S, int ld_kv, int k_col, int v_col, int bs, int n_q, int n_kv, int hd, float scale_log2,
+                            void* out, int ld_out, cudaStream_t st, const mk::SpLayout& sp = mk::SpLayout()) {
   const int G = n_q / n_kv;
   const int qpt = 128 / G;
-  if (S % (2 * qpt) || S % mk::TA_BK) return MK_ERR_BAD_SHAPE;
-  const int T = bs * S;
-  const auto* base = static_cast<const __nv_bfloat16*>(qkv);
+  if (rows % (2 * qpt) || S % mk::TA_BK) return MK_ERR_BAD_SHAPE;
+  if (sp.blk > 0 && (bs != 1 || sp.blk % (2 * qpt) || sp.blk % mk::TA_BK)) return MK_ERR_BAD_SHAPE;
+  const auto* qb = static_cast<const __nv_bfloat16*>(q_base);
+  const auto* kvb = static_cast<const __nv_bfloat16*>(kv_base);
   CUtensorMap mq, mkm, mv;
-  MK_TRY(map_heads(&mq, base + q_col, T, n_q, hd, ld_qkv, G, qpt));
-  MK_TRY(map_heads(&mkm, base + k_col, T, n_kv, hd, ld_qkv, 1, mk::TA_BK));
-  MK_TRY(map_heads(&mv, base + v_col, T, n_kv, hd, ld_qkv, 1, mk::TA_BK));
+  MK_TRY(map_heads(&mq, qb + q_col, bs * rows, n_q, hd, ld_q, G, qpt));
+  MK_TRY(map_heads(&mkm, kvb + k_col, bs * S, n_kv, hd, ld_kv, 1, mk::TA_BK));
+  MK_TRY(map_heads(&mv, kvb + v_col, bs * S, n_kv, hd, ld_kv, 1, mk::TA_BK));
   mk::AttnTcArgs a;
   a.S = S;
+  a.rows = rows;
+  a.sp = sp;
   a.lg2G = ilog2(G);
-  a.nqb = S / (2 * qpt);
+  a.nqb = rows / (2 * qpt);
   a.ld_out = ld_out;
   a.scale_log2 = scale_log2;
   a.err = d->err;
@@ -235,6 +243,12 @@ mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int 
   else
     mk::attn_tc_kernel<128><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
   return cuda_status(cudaGetLastError());
+}
+
+mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
+                      int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
+  return launch_attn_split(d, qkv, S, ld_qkv, q_col, qkv, S, ld_qkv, k_col, v_col, bs, n_q, n_kv, hd, scale_log2, out,
+                           ld_out, st);
 }
 
 mk_status check_attn_shape(int bs, int S, int n_q, int n_kv, int hd, int ld_qkv, int q_col, int k_col, int v_col,
@@ -596,6 +610,226 @@ mk_status mk_forward_timed(mk_handle* h, const int32_t* d_ids, int32_t bs, int32
   if (!times) return MK_ERR_BAD_ARG;
   StageClock clk;
   MK_TRY(forward_impl(h, d_ids, bs, seq, d_workspace, workspace_bytes, d_hidden, d_logits, d_top1, stream, &clk));
+  return clk.finish(times);
+}
+
+}  // extern "C"
+
+namespace {
+// Zig-zag block length for (seq, world); 0 if none fits.  A block holds whole attention query blocks
+// (2 * 128 / G rows), whole 64-key tiles and whole 32-token RoPE chunks.
+int sp_block(const mk_config& c, int seq, int world) {
+  if (world < 1 || seq <= 0 || c.n_kv <= 0) return 0;
+  const int min_blk = std::max(64, 256 / (c.n_q / c.n_kv));
+  for (int b = 512; b >= min_blk; b >>= 1)
+    if (seq % (2 * world * b) == 0) return b;
+  return 0;
+}
+
+struct SpWorkspace {
+  Workspace local;  // the single-sequence workspace of a rank's seq / world rows
+  size_t kv_send, kv_all, total;
+};
+
+SpWorkspace plan_workspace_sp(const mk_handle* h, int seq, int world) {
+  SpWorkspace w;
+  const int T = seq / world;
+  w.local = plan_workspace(h, 1, T);
+  const size_t kv_row = static_cast<size_t>(2 * h->kv_dim) * 2;
+  w.kv_send = w.local.total;
+  w.kv_all = align256(w.kv_send + T * kv_row);
+  w.total = align256(w.kv_all + static_cast<size_t>(seq) * kv_row);
+  return w;
+}
+
+mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32_t rank, int32_t world,
+                          mk_allgather_fn allgather, void* ctx, void* d_workspace, size_t workspace_bytes,
+                          void* d_hidden, float* d_logits, int32_t* d_top1, void* stream, StageClock* clk) {
+  if (!h || !d_ids || !d_workspace || !allgather) return MK_ERR_BAD_ARG;
+  if (world < 1 || rank < 0 || rank >= world) return MK_ERR_BAD_ARG;
+  if (!h->bound) return MK_ERR_NOT_BOUND;
+  const mk_config& c = h->cfg;
+  if (seq <= 0 || seq % 128 || seq > c.max_seq) return MK_ERR_BAD_SHAPE;
+  const int blk = sp_block(c, seq, world);
+  if (blk == 0) return MK_ERR_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(d_workspace) & 255u) || !aligned16(d_ids)) return MK_ERR_BAD_ALIGN;
+  if ((d_hidden && !aligned16(d_hidden)) || (d_logits && !aligned16(d_logits))) return MK_ERR_BAD_ALIGN;
+  const SpWorkspace sw = plan_workspace_sp(h, seq, world);
+  if (workspace_bytes < sw.total) return MK_ERR_WORKSPACE;
+  MK_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DeviceState* d = h->dev;
+  const Workspace& ws = sw.local;
+  uint8_t* base = static_cast<uint8_t*>(d_workspace);
+  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(base + off); };
+  auto f32 = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
+
+  const int L = c.num_layers, H = c.hidden, I = c.inter, hd = c.head_dim;
+  const int T = seq / world;  // this rank's rows
+  const int nqkv = h->n_qkv, qd = h->q_dim, kvd = h->kv_dim;
+  mk::SpLayout sp;
+  sp.blk = blk;
+  sp.rank = rank;
+  sp.world = world;
+  sp.rows_per_rank = T;
+  float *x32 = f32(ws.x32), *xl32 = f32(ws.xl32);
+  __nv_bfloat16 *xb = bf(ws.xb), *qkv = bf(ws.qkv), *attn = bf(ws.attn), *hb = bf(ws.hbuf);
+  __nv_bfloat16 *xlb = bf(ws.xlb), *ql = bf(ws.ql), *al = bf(ws.al), *hl = bf(ws.hl);
+  __nv_bfloat16 *kv_send = bf(sw.kv_send), *kv_all = bf(sw.kv_all);
+  float *rowsq = f32(ws.rowsq), *rowsql = f32(ws.rowsql), *hf = f32(ws.hf);
+  float* logits = d_logits ? d_logits : f32(ws.logits);
+  int32_t* top1 = d_top1 ? d_top1 : reinterpret_cast<int32_t*>(base + ws.top1);
+  const float r = c.residual_scale;
+  const size_t kv_row_bytes = static_cast<size_t>(2 * kvd) * 2;
+
+  CUtensorMap mx, mattn, mh, mxl, mal, mhl;
+  MK_TRY(map_a(&mx, xb, T, H, H));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd));
+  MK_TRY(map_a(&mh, hb, T, I, I));
+  MK_TRY(map_a(&mxl, xlb, 1, H, H));
+  MK_TRY(map_a(&mal, al, 1, qd, qd));
+  MK_TRY(map_a(&mhl, hl, 1, I, I));
+
+  auto mark = [&](int stage, int launches) { return clk ? clk->mark(stage, launches) : MK_OK; };
+  if (clk) MK_TRY(clk->start(st));
+  const int rows_per_blk = 8;
+  const int np = H / 128;
+  mk::embed_kernel<<<(T + rows_per_blk - 1) / rows_per_blk, 256, 0, st>>>(
+      d_ids, static_cast<const __nv_bfloat16*>(h->w.embed), x32, xb, T, H, c.vocab, c.scale_emb, d->err, rowsq, np,
+      sp);
+  MK_CUDA(cudaGetLastError());
+  MK_TRY(mark(MK_STAGE_EMBED, 1));
+
+  auto norm_from = [&](float* sq) {
+    GemmFusion f;
+    f.rowsq = sq;
+    f.rowsq_ld = np;
+    f.rowsq_np = np;
+    f.inv_norm_dim = 1.0f / static_cast<float>(H);
+    f.eps = c.eps;
+    return f;
+  };
+  // RoPE at the zig-zag positions of this rank's rows
+  auto with_rope_sp = [&](GemmFusion f, int cols) {
+    f.rope_cos = h->w.rope_cos;
+    f.rope_sin = h->w.rope_sin;
+    f.rope_cols = cols;
+    f.head_dim = hd;
+    f.rope_seq = seq;
+    f.rope_pos_base = 0;
+    f.sp = sp;
+    return f;
+  };
+  GemmFusion resid_stats;
+  resid_stats.rowsq = rowsq;
+  resid_stats.rowsq_ld = np;
+  GemmFusion resid_stats_last = resid_stats;
+  resid_stats_last.rowsq = rowsql;
+  // K/V columns of the local QKV rows -> packed send rows -> every rank's rows, rank by rank
+  auto gather_kv = [&](const __nv_bfloat16* src, int ld_src) -> mk_status {
+    MK_CUDA(cudaMemcpy2DAsync(kv_send, kv_row_bytes, src, static_cast<size_t>(ld_src) * 2, kv_row_bytes, T,
+                              cudaMemcpyDeviceToDevice, st));
+    if (allgather(ctx, kv_send, kv_all, static_cast<size_t>(T) * kv_row_bytes, stream) != 0) return MK_ERR_CUDA;
+    return MK_OK;
+  };
+
+  for (int l = 0; l < L - 1; ++l) {
+    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
+                       h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st, nullptr, 0,
+                       with_rope_sp(norm_from(rowsq), qd + kvd)));
+    MK_TRY(mark(MK_STAGE_QKV, 1));
+    MK_TRY(gather_kv(qkv + qd, nqkv));
+    MK_TRY(mark(MK_STAGE_KV_GATHER, 0));
+    MK_TRY(launch_attn_split(d, qkv, T, nqkv, 0, kv_all, seq, 2 * kvd, 0, kvd, 1, c.n_q, c.n_kv, hd, kLog2e, attn, qd,
+                             st, sp));
+    MK_TRY(mark(MK_STAGE_ATTN, 1));
+    MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
+                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+    MK_TRY(mark(MK_STAGE_O, 1));
+    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0, norm_from(rowsq)));
+    MK_TRY(mark(MK_STAGE_GATE_UP, 1));
+    MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+    MK_TRY(mark(MK_STAGE_DOWN, 1));
+  }
+
+  // Last layer: every rank projects K/V of its rows; rank 0 owns the last position (the second block
+  // of the last zig-zag group) and runs the rest for it.
+  {
+    const int l = L - 1;
+    const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
+    __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
+    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
+                       nullptr, 0, with_rope_sp(norm_from(rowsq), kvd)));
+    MK_TRY(mark(MK_STAGE_LAST_LAYER, 1));
+    MK_TRY(gather_kv(kv, 2 * kvd));
+    MK_TRY(mark(MK_STAGE_KV_GATHER, 0));
+    if (rank != 0) return MK_OK;
+    mk::gather_last_kernel<<<1, 256, 0, st>>>(x32, xl32, xlb, 1, T, H, rowsq, rowsql, np);
+    MK_CUDA(cudaGetLastError());
+    GemmFusion fq = norm_from(rowsql);
+    fq.rope_cos = h->w.rope_cos;
+    fq.rope_sin = h->w.rope_sin;
+    fq.rope_cols = qd;
+    fq.head_dim = hd;
+    fq.rope_seq = 1;
+    fq.rope_pos_base = seq - 1;
+    MK_TRY(launch_gemm(d, mxl, h->m_q_last, 1, qd, H, MK_GEMM_ROWSCALE, nullptr, sq, ql, qd, 0.f, st, nullptr, 0, fq));
+    AttnLastArgs la;
+    la.S = seq;
+    la.n_q = c.n_q;
+    la.n_kv = c.n_kv;
+    la.head_dim = hd;
+    la.ld_q = qd;
+    la.ld_kv = 2 * kvd;
+    la.k_col = 0;
+    la.v_col = kvd;
+    la.ld_out = qd;
+    la.scale_log2 = kLog2e;
+    la.sp = sp;
+    const size_t smem = static_cast<size_t>(seq) * 4;
+    if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
+    mk::attn_last_kernel<<<dim3(c.n_q, 1), 256, smem, st>>>(ql, kv_all, al, la);
+    MK_CUDA(cudaGetLastError());
+    MK_TRY(launch_gemm(d, mal, h->m_o[l], 1, H, qd, mk::GEMM_RESID32, nullptr,
+                       h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
+    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], 1, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
+    MK_TRY(launch_gemm(d, mhl, h->m_down[l], 1, H, I, mk::GEMM_RESID32, nullptr,
+                       h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
+    MK_TRY(mark(MK_STAGE_LAST_LAYER, 6));
+  }
+  mk::final_norm_kernel<<<1, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H, c.eps,
+                                           c.logit_scale);
+  MK_CUDA(cudaGetLastError());
+  MK_TRY(lm_head_launch(d, hf, 1, H, h->w.lm_head, c.vocab, logits, f32(ws.pval), reinterpret_cast<int*>(base + ws.pidx),
+                        top1, st));
+  return mark(MK_STAGE_HEAD, 3);
+}
+}  // namespace
+
+extern "C" {
+
+int32_t mk_sp_block(const mk_handle* h, int32_t seq, int32_t world) { return h ? sp_block(h->cfg, seq, world) : 0; }
+
+mk_status mk_workspace_size_sp(const mk_handle* h, int32_t seq, int32_t world, size_t* bytes) {
+  if (!h || !bytes) return MK_ERR_BAD_ARG;
+  if (world < 1) return MK_ERR_BAD_ARG;
+  if (sp_block(h->cfg, seq, world) == 0) return MK_ERR_BAD_SHAPE;
+  *bytes = plan_workspace_sp(h, seq, world).total;
+  return MK_OK;
+}
+
+mk_status mk_forward_sp(mk_handle* h, const int32_t* d_ids, int32_t seq, int32_t rank, int32_t world,
+                        mk_allgather_fn allgather, void* allgather_ctx, void* d_workspace, size_t workspace_bytes,
+                        void* d_hidden, float* d_logits, int32_t* d_top1, void* stream, mk_stage_times* times) {
+  if (!times)
+    return forward_sp_impl(h, d_ids, seq, rank, world, allgather, allgather_ctx, d_workspace, workspace_bytes, d_hidden,
+                           d_logits, d_top1, stream, nullptr);
+  StageClock clk;
+  MK_TRY(forward_sp_impl(h, d_ids, seq, rank, world, allgather, allgather_ctx, d_workspace, workspace_bytes, d_hidden,
+                         d_logits, d_top1, stream, &clk));
   return clk.finish(times);
 }
 

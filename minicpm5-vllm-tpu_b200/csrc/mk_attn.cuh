@@ -14,6 +14,7 @@ struct AttnLastArgs {
   int S, n_q, n_kv, head_dim;
   int ld_q, ld_kv, k_col, v_col, ld_out;
   float scale_log2;
+  SpLayout sp;  // sequence-parallel: kv is the rank-by-rank all-gather of one sequence (bs = 1)
 };
 
 __device__ __forceinline__ float block_reduce_max(float v, float* red) {
@@ -56,7 +57,7 @@ __global__ void __launch_bounds__(256)
   const __nv_bfloat16* vb = kv + static_cast<size_t>(b) * a.S * a.ld_kv + a.v_col + g * HD;
   float mx = -INFINITY;
   for (int j = tid; j < a.S; j += blockDim.x) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<size_t>(j) * a.ld_kv);
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<size_t>(sp_row(a.sp, j)) * a.ld_kv);
     float acc = 0.f;
     for (int c = 0; c < HD / 8; ++c) {
       const uint4 v = kr[c];
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(256)
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int j = warp; j < a.S; j += 8) {
     const float p = sc[j];
-    const __nv_bfloat16* vr = vb + static_cast<size_t>(j) * a.ld_kv;
+    const __nv_bfloat16* vr = vb + static_cast<size_t>(sp_row(a.sp, j)) * a.ld_kv;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int d = lane + 32 * e;

@@ -70,11 +70,15 @@ __device__ __forceinline__ float exp2_fma(float x) {
 }
 
 struct AttnTcArgs {
-  int S;       // sequence length
+  int S;       // sequence length (K/V rows per sequence)
+  int rows;    // query / output rows per sequence (S, or a rank's rows under sequence parallelism)
   int lg2G;    // log2(query heads per KV head)
-  int nqb;     // query blocks (of 2 * 128/G queries) per sequence
+  int nqb;     // query blocks (of 2 * 128/G queries) per sequence: rows / (2 * 128/G)
   int ld_out;  // elements per output row
   float scale_log2;
+  // Sequence parallelism (sp.blk > 0, bs = 1): the query rows are this rank's zig-zag rows (row m at
+  // position sp_pos(sp, m)) and K/V is the rank-by-rank all-gather (position p at row sp_row(sp, p)).
+  SpLayout sp;
   int* err;
 };
 
@@ -105,9 +109,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   const int G = 1 << a.lg2G;
   const int qpt = 128 >> a.lg2G;  // queries per Q tile
   const int qb = a.nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
-  const int q0 = qb * 2 * qpt;
+  const int qrow0 = qb * 2 * qpt;      // first query row of the CTA (local)
+  const int q0 = sp_pos(a.sp, qrow0);  // its position; the 2 * qpt rows share one zig-zag block
   const int g = blockIdx.y;
-  const int tok0 = blockIdx.z * a.S;
+  const int tok0 = blockIdx.z * a.rows;  // query / output rows of this sequence
+  const int kv0 = blockIdx.z * a.S;      // K/V rows of this sequence
   const int ntiles = (q0 + 2 * qpt - 1) / TA_BK + 1;
 
   if (threadIdx.x == 0) {
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       mbar_arrive_expect_tx(q_full, 4 * TA_QCHUNK);
       for (int t = 0; t < 2; ++t)
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(sQ + (t * 2 + c) * TA_QCHUNK, &tmQ, q_full, c * 64, g * G, tok0 + q0 + t * qpt);
+          tma_load_3d(sQ + (t * 2 + c) * TA_QCHUNK, &tmQ, q_full, c * 64, g * G, tok0 + qrow0 + t * qpt);
     }
     __syncwarp();
     for (int j = 0; j < ntiles; ++j) {
@@ -160,10 +166,12 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       uint8_t* sst = sKV + st * TA_STAGE;
       if (leader) {
         mbar_arrive_expect_tx(&k_full[st], 2 * TA_KCHUNK);
-        for (int c = 0; c < 2; ++c) tma_load_3d(sst + c * TA_KCHUNK, &tmK, &k_full[st], c * 64, g, tok0 + j * TA_BK);
+        // a 64-key tile never straddles a zig-zag block (blocks are multiples of 64 tokens)
+        const int krow = kv0 + sp_row(a.sp, j * TA_BK);
+        for (int c = 0; c < 2; ++c) tma_load_3d(sst + c * TA_KCHUNK, &tmK, &k_full[st], c * 64, g, krow);
         mbar_arrive_expect_tx(&v_full[st], 2 * TA_KCHUNK);
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(sst + (2 + c) * TA_KCHUNK, &tmV, &v_full[st], c * 64, g, tok0 + j * TA_BK);
+          tma_load_3d(sst + (2 + c) * TA_KCHUNK, &tmV, &v_full[st], c * 64, g, krow);
       }
       __syncwarp();
       issued |= 1u << st;
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     if (ok && mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag)) {
       tc_fence_after();
       const float inv = 1.f / l;
-      __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + query) * a.ld_out + head * HD;
+      __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + qrow0 + (query - q0)) * a.ld_out + head * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o32[32];

@@ -27,6 +27,33 @@ enum : int {
 // Wall-clock limit of one mbarrier wait.  Legitimate waits are microseconds long.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Zig-zag sequence-parallel layout of one sequence over `world` ranks (sp_global_block,
+// plugin/minicpm5_mk/mk_attn.py:721-724, generalised from 2 to `world` ranks): the sequence is cut
+// into blocks of `blk` tokens; in every group of 2 * world consecutive blocks, rank r owns block r
+// and block 2 * world - 1 - r, which balances the causal attention work.  A rank stores its blocks
+// in sequence order (`rows_per_rank` rows); an all-gather stacks the ranks' rows rank by rank.
+// blk == 0 is the identity (one rank, rows = positions).
+struct SpLayout {
+  int blk = 0, rank = 0, world = 1, rows_per_rank = 0;
+};
+
+// Sequence position of local row `row`.
+__host__ __device__ __forceinline__ int sp_pos(const SpLayout& l, int row) {
+  if (l.blk == 0) return row;
+  const int i = row / l.blk, k = i >> 1;
+  const int b = 2 * l.world * k + ((i & 1) ? 2 * l.world - 1 - l.rank : l.rank);
+  return b * l.blk + row % l.blk;
+}
+
+// Row of sequence position `pos` in the rank-by-rank all-gathered buffer.
+__host__ __device__ __forceinline__ int sp_row(const SpLayout& l, int pos) {
+  if (l.blk == 0) return pos;
+  const int b = pos / l.blk, k = b / (2 * l.world), m = b % (2 * l.world);
+  const bool second = m >= l.world;
+  const int r = second ? 2 * l.world - 1 - m : m;
+  return r * l.rows_per_rank + (2 * k + (second ? 1 : 0)) * l.blk + pos % l.blk;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

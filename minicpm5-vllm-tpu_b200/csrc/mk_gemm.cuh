@@ -103,6 +103,9 @@ struct GemmArgs {
   const float* rope_cos;
   const float* rope_sin;
   int rope_cols, head_dim, rope_seq, rope_pos_base;
+  // Sequence-parallel rows (sp.blk > 0): token m is local row m of one zig-zag sequence, at
+  // position sp_pos(sp, m); rope_seq is then the whole sequence's length and rope_pos_base 0.
+  SpLayout sp;
   int* err;
 };
 
@@ -408,7 +411,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
           if (rope) {
             const bool odd = (lane & 1) != 0;
-            const int p0 = args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
+            // zig-zag blocks are multiples of 32 tokens, so a chunk's positions stay consecutive
+            const int p0 = args.sp.blk > 0 ? sp_pos(args.sp, tokc) : args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
             if (args.rope_seq >= 32 && p0 + 32 <= args.rope_seq) {
               // The chunk's 32 tokens have consecutive positions: (cos, sin) of the pair's angle at
               // each position follow from the previous one by the angle-addition rotation with the
@@ -441,7 +445,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                   const int j = hb + jj < jn ? hb + jj : 0;
-                  const int pos = (tokc + j) % args.rope_seq;
+                  const int pos = args.sp.blk > 0 ? sp_pos(args.sp, tokc + j) : (tokc + j) % args.rope_seq;
                   const size_t e = static_cast<size_t>(pos + args.rope_pos_base) * hh + pj;
                   cv[jj] = __ldg(args.rope_cos + e);
                   sv[jj] = __ldg(args.rope_sin + e);

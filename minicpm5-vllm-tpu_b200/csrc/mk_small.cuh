@@ -12,11 +12,12 @@ namespace mk {
 // DEV_ERR_BAD_TOKEN_ID.
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
                              float* __restrict__ x32, __nv_bfloat16* __restrict__ xb, int T, int H, int V, float scale,
-                             int* err, float* __restrict__ rowsq = nullptr, int rowsq_ld = 0) {
+                             int* err, float* __restrict__ rowsq = nullptr, int rowsq_ld = 0,
+                             SpLayout sp = SpLayout()) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
-  const int id = ids[row];
+  const int id = ids[sp_pos(sp, row)];  // sequence-parallel: ids are the whole sequence's
   uint4* db = reinterpret_cast<uint4*>(xb + static_cast<size_t>(row) * H);
   float4* d32 = reinterpret_cast<float4*>(x32 + static_cast<size_t>(row) * H);
   if (rowsq)  // fused RMSNorm statistics: the whole row's sum of squares in slot 0, other slots 0

@@ -16,7 +16,7 @@ EXPORTED = (
     "mk_status_string", "mk_version", "mk_create", "mk_bind_weights", "mk_workspace_size", "mk_forward",
     "mk_get_error", "mk_destroy", "mk_gemm_w8a16", "mk_attention_prefill", "mk_rope", "mk_rms_rstd", "mk_embed",
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward", "mk_lm_head_argmax_noalloc",
-    "mk_topk_logprobs", "mk_forward_timed",
+    "mk_topk_logprobs", "mk_forward_timed", "mk_sp_block", "mk_workspace_size_sp", "mk_forward_sp",
 )
 
 MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
@@ -35,7 +35,11 @@ class MkWeightPtrsC(ctypes.Structure):
                                    "w_o", "s_o", "w_gu", "s_gu", "w_down", "s_down")]
 
 
-MK_STAGE_NAMES = ("embed", "qkv", "attn", "o_proj", "gate_up", "down", "last_layer", "head")
+MK_STAGE_NAMES = ("embed", "qkv", "attn", "o_proj", "gate_up", "down", "last_layer", "head", "kv_gather")
+
+# int32 (*)(void* ctx, const void* d_send, void* d_recv, size_t bytes_per_rank, void* stream)
+ALLGATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                ctypes.c_void_p)
 
 
 class MkStageTimesC(ctypes.Structure):
@@ -68,6 +72,11 @@ def lib() -> ctypes.CDLL:
         L.mk_forward.argtypes = [_vp, _vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _vp]
         L.mk_forward_timed.argtypes = [_vp, _vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _vp,
                                        ctypes.POINTER(MkStageTimesC)]
+        L.mk_sp_block.restype = _i32
+        L.mk_sp_block.argtypes = [_vp, _i32, _i32]
+        L.mk_workspace_size_sp.argtypes = [_vp, _i32, _i32, ctypes.POINTER(_sz)]
+        L.mk_forward_sp.argtypes = [_vp, _vp, _i32, _i32, _i32, ALLGATHER_FN, _vp, _vp, _sz, _vp, _vp, _vp, _vp,
+                                    ctypes.POINTER(MkStageTimesC)]
         L.mk_get_error.argtypes = [_vp, ctypes.POINTER(_i32)]
         L.mk_destroy.restype = None
         L.mk_destroy.argtypes = [_vp]

@@ -109,6 +109,59 @@ class MkEngine:
                 stage_times[name] = {"ms": float(t.ms[i]), "launches": int(t.launches[i])}
         return hid, lg, top1
 
+    # ------------------------------------------------------------------ sequence parallelism
+    def sp_block(self, seq: int, world: int) -> int:
+        return int(_lib.lib().mk_sp_block(self._h, seq, world))
+
+    def sp_workspace(self, seq: int, world: int) -> torch.Tensor:
+        """The workspace mk_forward_sp uses (shared with `forward`'s): bind the all-gather callback to it."""
+        n = ctypes.c_size_t()
+        _lib.check(_lib.lib().mk_workspace_size_sp(self._h, seq, world, ctypes.byref(n)), "mk_workspace_size_sp")
+        if self._ws is None or self._ws.numel() < n.value:
+            self._ws = None
+            self._ws = torch.empty(int(n.value), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward_sp(self, ids: torch.Tensor, seq: int, rank: int, world: int, gather, *,
+                   out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+                   stage_times: Optional[dict] = None):
+        """Sequence-parallel forward of one sequence through `mk_forward_sp`.  `ids`: int32 [seq] (the whole
+        sequence, on every rank).  `gather(send_ptr, recv_ptr, bytes_per_rank, stream) -> 0` is the
+        all-gather over the workspace from `sp_workspace` (minicpm5_mk.sp builds one).  Returns
+        (hidden, logits, top1) as `forward` with bs = 1; they are written on rank 0 only."""
+        _cuda(ids, "ids")
+        if ids.dtype != torch.int32 or ids.numel() < seq:
+            raise ValueError("minicpm5_mk: ids must be int32 with at least seq entries")
+        ws = self.sp_workspace(seq, world)
+        if out is not None:
+            hid, lg, top1 = out
+        else:
+            hid = torch.empty((1, self.cfg.hidden), dtype=torch.bfloat16, device=self.device)
+            lg = torch.empty((1, self.cfg.vocab), dtype=torch.float32, device=self.device)
+            top1 = torch.empty((1,), dtype=torch.int32, device=self.device)
+        failure = []
+
+        def cb(ctx, send, recv, nbytes, stream):
+            try:
+                return int(gather(int(send), int(recv), int(nbytes), int(stream or 0)))
+            except BaseException as e:  # an exception must not cross the C frames
+                failure.append(e)
+                return 1
+
+        fn = _lib.ALLGATHER_FN(cb)
+        t = _lib.MkStageTimesC() if stage_times is not None else None
+        st = _lib.lib().mk_forward_sp(self._h, ids.data_ptr(), seq, rank, world, fn, None, ws.data_ptr(), ws.numel(),
+                                      _ptr(hid), _ptr(lg), top1.data_ptr(), _stream(self.device),
+                                      ctypes.byref(t) if t is not None else None)
+        if failure:
+            raise RuntimeError("minicpm5_mk: sequence-parallel all-gather failed") from failure[0]
+        _lib.check(st, "mk_forward_sp")
+        if t is not None:
+            stage_times.clear()
+            for i, name in enumerate(_lib.MK_STAGE_NAMES):
+                stage_times[name] = {"ms": float(t.ms[i]), "launches": int(t.launches[i])}
+        return hid, lg, top1
+
     def launches_per_forward(self, bs: int, seq: int) -> int:
         return int(_lib.lib().mk_launches_per_forward(self._h, bs, seq))
 
