@@ -48,6 +48,7 @@ def _args():
     ap.add_argument("--latency-runs", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sp", action="store_true", help="skip the sequence-parallel 1 x seq latency (N > 1)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_kv", "gemm_down", "attn"],
                     help="time one isolated kernel of the forward (profiling driver) instead of the bench")
@@ -430,6 +431,46 @@ def main():
                "timing": "device (CUDA events)"}
     barrier()
 
+    # ---------------------------------------------------------------- latency at 1 x seq, sequence parallel
+    # One sequence over all N ranks (zig-zag blocks, per-layer K/V all-gather over NCCL): every rank runs
+    # every step; a run's latency is the maximum over ranks of its device time.
+    lat_sp = None
+    if world > 1 and not a.no_sp and a.latency_runs > 0 and eng.sp_block(S, world) > 0:
+        from minicpm5_mk import sp as mk_sp
+        one_sp = synthetic_ids(1, S, seed=1234).reshape(-1).contiguous().to(dev)  # the same sequence on every rank
+        gather = mk_sp.nccl_allgather()(eng.sp_workspace(S, world))
+        o1 = (hid[:1], lg[:1], top1[:1])
+        for _ in range(5):
+            eng.forward_sp(one_sp, S, rank, world, gather, out=o1)
+        torch.cuda.synchronize()
+        barrier()
+        ts_sp = []
+        for _ in range(a.latency_runs):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            eng.forward_sp(one_sp, S, rank, world, gather, out=o1)
+            s1.record(stream)
+            s1.synchronize()
+            ts_sp.append(s0.elapsed_time(s1))
+        t = torch.tensor(ts_sp, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ts_sp = sorted(t.tolist())
+        sp_stages = {}
+        eng.forward_sp(one_sp, S, rank, world, gather, out=o1, stage_times=sp_stages)
+        barrier()
+
+        def pct_sp(p):
+            k = (len(ts_sp) - 1) * p / 100.0
+            lo = int(k)
+            hi = min(lo + 1, len(ts_sp) - 1)
+            return ts_sp[lo] + (ts_sp[hi] - ts_sp[lo]) * (k - lo)
+
+        lat_sp = {"p50_ms": round(pct_sp(50), 3), "p99_ms": round(pct_sp(99), 3), "runs": len(ts_sp), "warmup": 5,
+                  "ranks": world, "block": eng.sp_block(S, world),
+                  "timing": "device (CUDA events), max over ranks per run",
+                  "api": "minicpm5_mk.ops.MkEngine.forward_sp -> mk_forward_sp (C ABI) + NCCL all-gather",
+                  "stages_rank0_ms": {k: round(v["ms"], 3) for k, v in sp_stages.items()}}
+
     # ---------------------------------------------------------------- roofline of the dominant kernels
     # In-step figures: each stage's device time inside the forward just after the timed region (a long,
     # power-capped step), against the sustained GEMM peak.  Alone figures: the two largest kernels timed
@@ -514,7 +555,8 @@ def main():
         "model_roofline_peak": "sustained bf16 GEMM peak per GPU",
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": eng.launches_per_forward(bs, S) * a.steps,
-        "clocks": clocks, "latency_1x8192": lat, "device_error": err,
+        "clocks": clocks, "latency_1x8192": lat,
+        "latency_1x8192_sp": lat_sp, "device_error": err,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
