@@ -438,7 +438,7 @@ def main():
     if world > 1 and not a.no_sp and a.latency_runs > 0 and eng.sp_block(S, world) > 0:
         from minicpm5_mk import sp as mk_sp
         one_sp = synthetic_ids(1, S, seed=1234).reshape(-1).contiguous().to(dev)  # the same sequence on every rank
-        gather = mk_sp.nccl_allgather()(eng.sp_workspace(S, world))
+        gather = mk_sp.nccl_allgather()
         o1 = (hid[:1], lg[:1], top1[:1])
         for _ in range(5):
             eng.forward_sp(one_sp, S, rank, world, gather, out=o1)

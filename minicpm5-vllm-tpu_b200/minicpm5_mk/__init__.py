@@ -38,3 +38,7 @@ def register() -> None:
 
     if ARCH not in ModelRegistry.get_supported_archs():
         ModelRegistry.register_model(ARCH, "minicpm5_mk.model:MiniCPM5MegakernelForCausalLM")
+    # engine hooks for max_tokens=1 scoring batches (plugin/minicpm5_mk/__init__.py:154-244)
+    from .engine_hooks import install
+
+    install()

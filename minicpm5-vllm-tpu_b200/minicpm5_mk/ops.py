@@ -122,17 +122,19 @@ class MkEngine:
             self._ws = torch.empty(int(n.value), dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def forward_sp(self, ids: torch.Tensor, seq: int, rank: int, world: int, gather, *,
+    def forward_sp(self, ids: torch.Tensor, seq: int, rank: int, world: int, gather_for, *,
                    out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
                    stage_times: Optional[dict] = None):
         """Sequence-parallel forward of one sequence through `mk_forward_sp`.  `ids`: int32 [seq] (the whole
-        sequence, on every rank).  `gather(send_ptr, recv_ptr, bytes_per_rank, stream) -> 0` is the
-        all-gather over the workspace from `sp_workspace` (minicpm5_mk.sp builds one).  Returns
-        (hidden, logits, top1) as `forward` with bs = 1; they are written on rank 0 only."""
+        sequence, on every rank).  `gather_for(workspace)` returns the all-gather the library calls,
+        `gather(send_ptr, recv_ptr, bytes_per_rank, stream) -> 0`, over that uint8 workspace tensor
+        (minicpm5_mk.sp.nccl_allgather / ThreadGroup build them).  Returns (hidden, logits, top1) as
+        `forward` with bs = 1; they are written on rank 0 only."""
         _cuda(ids, "ids")
         if ids.dtype != torch.int32 or ids.numel() < seq:
             raise ValueError("minicpm5_mk: ids must be int32 with at least seq entries")
         ws = self.sp_workspace(seq, world)
+        gather = gather_for(ws)
         if out is not None:
             hid, lg, top1 = out
         else:

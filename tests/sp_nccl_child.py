@@ -22,8 +22,7 @@ def main():
     cfg = get_config("minicpm5-1b").replace(max_seq=8192)
     eng = MkEngine(cfg, mk_weights.prepare_mk_weights(random_state_dict(cfg, seed=1234, device=dev), cfg), dev)
     ids = synthetic_ids(1, 8192, seed=1234).reshape(-1).contiguous().to(dev)
-    ws = eng.sp_workspace(8192, world)
-    h1, l1, t1 = eng.forward_sp(ids, 8192, rank, world, sp.nccl_allgather()(ws))
+    h1, l1, t1 = eng.forward_sp(ids, 8192, rank, world, sp.nccl_allgather())
     torch.cuda.synchronize()
     ok = True
     if rank == 0:

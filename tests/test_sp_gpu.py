@@ -34,13 +34,12 @@ def _run_threads(engines, ids, seq, world):
     tg = sp.ThreadGroup(world)
     outs, errs = [None] * world, []
     streams = [torch.cuda.Stream() for _ in range(world)]
-    wss = [e.sp_workspace(seq, world) for e in engines]
     torch.cuda.synchronize()
 
     def rank_main(r):
         try:
             with torch.cuda.stream(streams[r]):
-                outs[r] = engines[r].forward_sp(ids, seq, r, world, tg.bind(r, wss[r], streams[r]))
+                outs[r] = engines[r].forward_sp(ids, seq, r, world, lambda ws: tg.bind(r, ws, streams[r]))
         except BaseException as e:  # noqa: BLE001
             errs.append(e)
             tg.abort()
@@ -87,12 +86,11 @@ def test_sp_stage_times_and_errors():
     cfg = PRESETS["tiny-hd96"]
     base, _ = _engines(cfg, 1)
     ids = synthetic_ids(1, 1024, seed=3, vocab=cfg.vocab).reshape(-1).contiguous().cuda()
-    ws = base.sp_workspace(1024, 1)
-    stream = torch.cuda.current_stream()
-
-    def local(send, recv, nbytes, s):  # world 1: the gather is a copy
-        sp._slice(ws, recv, nbytes).copy_(sp._slice(ws, send, nbytes))
-        return 0
+    def local(ws):  # world 1: the gather is a copy
+        def gather(send, recv, nbytes, s):
+            sp._slice(ws, recv, nbytes).copy_(sp._slice(ws, send, nbytes))
+            return 0
+        return gather
 
     stages = {}
     h1, l1, t1 = base.forward_sp(ids, 1024, 0, 1, local, stage_times=stages)
@@ -101,13 +99,12 @@ def test_sp_stage_times_and_errors():
     assert torch.equal(l0, l1)
     assert stages["attn"]["launches"] == cfg.num_layers - 1 and stages["kv_gather"]["ms"] > 0
     with pytest.raises(RuntimeError):  # a failing collective surfaces as an error, not a hang
-        base.forward_sp(ids, 1024, 0, 1, lambda *a: 1 / 0)
+        base.forward_sp(ids, 1024, 0, 1, lambda ws: lambda *a: 1 / 0)
     from minicpm5_mk._lib import MkError
     with pytest.raises(MkError):
         base.forward_sp(ids, 1024, 1, 1, local)  # rank outside the world
     with pytest.raises(MkError):
         base.forward_sp(ids, 1024, 0, 16, local)  # no zig-zag block fits
-    del stream
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs on one node")

@@ -26,16 +26,29 @@ def _child(what, mdir, timeout):
     r = subprocess.run([sys.executable, os.path.join(HERE, "vllm_drop_in_child.py"), what, mdir], env=env,
                        capture_output=True, text=True, timeout=timeout)
     assert r.returncode == 0, (what, r.stdout[-2000:], r.stderr[-4000:])
-    return json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    return json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1]), r.stdout + r.stderr
 
 
 def test_vllm_generate_drop_in(tmp_path):
     pytest.importorskip("vllm")
     mdir = str(tmp_path / "tiny_llama")
-    made = _child("make", mdir, 300)
-    fast = _child("mk", mdir, 600)
-    stock = _child("stock", mdir, 600)
+    made, _ = _child("make", mdir, 300)
+    fast, _ = _child("mk", mdir, 600)
+    stock, _ = _child("stock", mdir, 600)
     assert fast["tokens"] == made["golden_top1"], (fast, made)
     assert stock["tokens"] == made["golden_top1"], (stock, made)
     served = fast["status"]["shapes"]
     assert served and all(k.startswith("mk:") for k in served), fast["status"]
+
+
+def test_vllm_generate_kv_cache_skip(tmp_path):
+    """With no stock fallback (MINICPM5_MK_FREE_STOCK=1) the scheduler hands the max_tokens=1 prefills no
+    KV-cache blocks (engine hook of plugin/minicpm5_mk/__init__.py:154-205) and the tokens stay the golden's."""
+    pytest.importorskip("vllm")
+    mdir = str(tmp_path / "tiny_llama")
+    made, _ = _child("make", mdir, 300)
+    free, log = _child("mkfree", mdir, 600)
+    assert free["tokens"] == made["golden_top1"], (free, made)
+    assert "KV-cache allocation skipped" in log
+    served = free["status"]["shapes"]
+    assert served and all(k.startswith("mk:") for k in served), free["status"]

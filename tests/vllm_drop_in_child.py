@@ -3,6 +3,7 @@
     python tests/vllm_drop_in_child.py make <dir>    # tiny Llama-format checkpoint + prompts + golden top-1
     python tests/vllm_drop_in_child.py mk <dir>      # LLM.generate through MiniCPM5MegakernelForCausalLM
     python tests/vllm_drop_in_child.py stock <dir>   # same, MINICPM5_MK_ENABLE=0 (vLLM's own Llama path)
+    python tests/vllm_drop_in_child.py mkfree <dir>  # plugin path with MINICPM5_MK_FREE_STOCK=1 (KV-cache skip)
 
 Prints one JSON line.  The checkpoint is the tiny-hd96 preset with plain-Llama scalars (the muP
 scalars at 1.0, so vLLM's stock Llama and the megakernel compute the same model), random weights
@@ -44,9 +45,11 @@ def make(mdir):
     print(json.dumps({"made": mdir, "golden_top1": top1}))
 
 
-def generate(mdir, fast):
+def generate(mdir, fast, free_stock=False):
     if fast:
         os.environ["MINICPM5_MK_STATUS_DIR"] = os.path.join(mdir, "status")
+        if free_stock:  # no stock fallback: the KV-cache allocation skip applies
+            os.environ["MINICPM5_MK_FREE_STOCK"] = "1"
     else:
         os.environ["MINICPM5_MK_ENABLE"] = "0"
     from vllm import LLM, SamplingParams
@@ -69,4 +72,4 @@ if __name__ == "__main__":
     if what == "make":
         make(mdir)
     else:
-        generate(mdir, what == "mk")
+        generate(mdir, what in ("mk", "mkfree"), free_stock=what == "mkfree")
