@@ -321,6 +321,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         mx4[(e >> 1) & 3] = max3f(mx4[(e >> 1) & 3], __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
       const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
       const bool need = m_tile > m_used + TA_RESCALE_THRESHOLD;
+      bool prev_pv_waited = false;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O_t += P_t V of the previous tile must have landed before O_t is rescaled
         if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag)) {
@@ -328,6 +329,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           break;
         }
         tc_fence_after();
+        prev_pv_waited = true;
         const float alpha = need ? ex2_approx(m_used - m_tile) : 1.f;
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
@@ -356,6 +358,16 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         pk[e] = pack_bf16x2(p0, p1);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      if (j == ntiles - 1 && j > 0 && !prev_pv_waited) {
+        // pv_done is a parity barrier: a wait is only exact while at most one completion is
+        // outstanding.  The epilogue waits for O_t += P_t(last) V; completing the wait for the
+        // second-to-last one here (before P_t(last) is handed over, so nothing later can be issued)
+        // leaves exactly one outstanding.
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+      }
       tmem_st_32x32b_x32(tS + b * 64, pk);  // P_t(j) over the S columns just read
       tmem_st_wait();
       tc_fence_before();
