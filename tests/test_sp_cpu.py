@@ -131,6 +131,42 @@ def test_allgather_callback_two_gloo_ranks():
         assert rest == 0
 
 
+def _worker_dead_peer(rank, world, port, q):
+    """Rank 1 leaves before the gather; rank 0's gather must fail within the group timeout, not hang."""
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        q.put((1, "left"))
+        q.close()
+        q.join_thread()  # the message is out before the process vanishes
+        os._exit(0)  # no destroy, no gather: the peer just disappears
+    ws = torch.zeros(1024, dtype=torch.uint8)
+    gather = sp.nccl_allgather()(ws)
+    try:
+        gather(ws.data_ptr(), ws.data_ptr() + 256, 100, 0)
+        q.put((0, "returned"))
+    except Exception as e:  # noqa: BLE001 - any error is the expected outcome
+        q.put((0, "error: " + type(e).__name__))
+
+
+def test_allgather_with_a_dead_peer_errors_out():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_dead_peer, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("error"), res
+
+
 def test_allgather_rejects_buffers_outside_the_workspace():
     ws = torch.zeros(64, dtype=torch.uint8)
     with pytest.raises(ValueError):
