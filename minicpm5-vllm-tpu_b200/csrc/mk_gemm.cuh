@@ -28,19 +28,24 @@
 // residual (plugin/minicpm5_mk/mk_jax.py:233-269, :394), `fused_mlp`
 // (plugin/minicpm5_mk/mk_mlp.py:68-145).
 //
-// CTA layout (persistent, one CTA per SM, 15 warps).  Tile = 128 output channels x nt tokens
-// (nt = 192, or the token count rounded up to 16 when M is smaller):
-//   warp 0 lane 0 : TMA producer of the token tiles (nt x 64 bf16, 128B swizzle), 6-slot ring
-//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=nt, K=16, A in TMEM)
-//   warp 2 lane 0 : TMA producer of the int8 weight tiles (128 x 64, 64B swizzle), 6-slot ring
+// CTA layout (persistent, one CTA per SM, 19 warps).  Tile = 128 output channels x nt tokens
+// (nt = 192, or the token count rounded up to 16 when M is smaller); one pipeline stage covers 128 of K:
+//   warp 0        : TMA producer of the token tiles (two nt x 64 bf16 panels per stage, 128B swizzle),
+//                   3-slot ring; the warp runs the loop, one elected lane issues
+//   warp 1        : TMEM allocator + tcgen05.mma issuer (M=128, N=nt, K=16, A in TMEM); the whole warp
+//                   runs the loop (descriptors in uniform registers), one elected lane issues
+//   warp 2        : TMA producer of the int8 weight tiles (128 x 128 B, 128B swizzle), 3-slot ring,
+//                   run the same way as warp 0
 //   warps 3..10   : epilogue (TMEM -> registers -> global), two warps per 32-lane TMEM quarter
 //                   (= 32 output channels) taking alternate 32-token chunks; thread = channel,
 //                   registers = consecutive tokens, so every global access of a warp covers 32
 //                   consecutive channels of one token row
-//   warps 11..14  : int8 -> bf16 converters: shared memory -> registers -> tcgen05.st into a
-//                   4-slot TMEM weight ring (one warp per TMEM lane quarter)
+//   warps 11..18  : int8 -> bf16 converters, two per TMEM lane quarter (one half of the stage's K
+//                   each): shared memory -> registers -> tcgen05.st into a 2-slot TMEM weight ring
+// A warp can only reach the TMEM lane quarter of its SM sub-partition (warp slot mod 4), which fixes
+// which quarter each epilogue and converter warp serves.
 // TMEM (512 columns): two f32 accumulators of 192 columns (the epilogue of tile i overlaps the main
-// loop of tile i+1) + 4 weight slots of 32 columns (128 x 64 bf16, two K values per column).
+// loop of tile i+1) + 2 weight slots of 64 columns (128 x 128 bf16, two K values per column).
 #pragma once
 
 #include "mk_common.cuh"
