@@ -53,7 +53,7 @@ template <int HD>
 __host__ __device__ constexpr int ta_q_tmem_ksteps() { return HD == 96 ? 4 : 0; }
 
 // Pairs of softmax exponentials e with (e & TA_FMA_EXP_MASK) == TA_FMA_EXP_MASK go to the FMA pipe.
-constexpr int TA_FMA_EXP_MASK = 7;
+constexpr int TA_FMA_EXP_MASK = 15;
 
 // 2^x on the FMA pipe for a share of the softmax exponentials: 16 MUFU results per clock per SM
 // cannot keep up with the tensor core at head_dim 96.  x = j + f with j = round(x) (adding
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       for (int e = 0; e < 32; ++e) {
         float x0, x1;
         fma2_sc(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]), sc, -m_used, x0, x1);
-        // an eighth of the exponentials on the FMA pipe, the rest on MUFU
+        // a sixteenth of the exponentials on the FMA pipe, the rest on MUFU
         const bool fma_exp = HD == 96 && (e & TA_FMA_EXP_MASK) == TA_FMA_EXP_MASK;
         const float p0 = fma_exp ? exp2_fma(x0) : ex2_approx(x0);
         const float p1 = fma_exp ? exp2_fma(x1) : ex2_approx(x1);
