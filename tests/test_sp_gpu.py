@@ -71,12 +71,14 @@ def test_sp_threads_bit_identical_tiny(preset, seq, world):
         assert e.check_device_error() == 0
 
 
-def test_sp_threads_bit_identical_1b_s8192():
+@pytest.mark.parametrize("world", [2, 8])
+def test_sp_threads_bit_identical_1b_s8192(world):
+    """The BASELINE config at the 2- and 8-GPU layouts (8 ranks: 1024 rows each, 64 attention CTAs)."""
     cfg = get_config("minicpm5-1b").replace(max_seq=8192)
-    base, engines = _engines(cfg, 2)
+    base, engines = _engines(cfg, world)
     ids = synthetic_ids(1, 8192, seed=1234).reshape(-1).contiguous().cuda()
     h0, l0, t0 = base.forward(ids, 1, 8192)
-    h1, l1, t1 = _run_threads(engines, ids, 8192, 2)
+    h1, l1, t1 = _run_threads(engines, ids, 8192, world)
     assert torch.equal(t0, t1)
     assert torch.equal(l0, l1)
     assert torch.equal(h0, h1)
