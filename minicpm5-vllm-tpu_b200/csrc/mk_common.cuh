@@ -369,6 +369,13 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
   return __bfloat1622float2(v);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+// silu(g) = g * sigmoid(g), with sigmoid(g) = (1 + tanh(g / 2)) / 2: one MUFU operation (tanh.approx,
+// relative error about 2^-11, below the bf16 rounding of the result) instead of an exponential and a
+// reciprocal.  Measured 1 % faster on the gate/up GEMM, cold and under the power cap.
+__device__ __forceinline__ float silu_f(float g) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+  return 0.5f * g * (1.0f + t);
+}
 
 }  // namespace mk
