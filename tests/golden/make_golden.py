@@ -2,7 +2,7 @@
 
 Run in the build container (it reads the reference sources, which do not exist on the GPU box):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 1. `f32_golden.forward_one` (benchmark/f32_golden.py:78-102) of the reference, executed with the
    numpy stand-in for jax under tests/golden/jax_shim, on small seeded random-init models
@@ -131,7 +131,7 @@ def make_gate(ref_root):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--only", default="f32,quant,gate")
     a = ap.parse_args()
     only = set(a.only.split(","))
