@@ -21,17 +21,23 @@ from typing import Dict, List, Tuple
 
 import torch
 
-from .mk_config import MkConfig, from_hf_config
+from .mk_config import MkConfig, from_hf_config, rope_support
 
 
 def load_hf_checkpoint(path: str, device: str | torch.device = "cpu",
                        max_seq: int = 8192) -> Tuple[MkConfig, Dict[str, torch.Tensor]]:
     """(config, state dict) of the checkpoint directory `path`.  Tensors keep their stored dtype; they are
-    read onto `device` (a CUDA device makes `prepare_mk_weights` run on the GPU)."""
+    read onto `device` (a CUDA device makes `prepare_mk_weights` run on the GPU).  rope_theta is read from
+    `rope_parameters` / `rope_scaling` where the config keeps it there; a rope type other than plain RoPE
+    (yarn, longrope, ...) raises ValueError, as the vLLM model class disables its fast path for it."""
     cfg_path = os.path.join(path, "config.json")
     if not os.path.exists(cfg_path):
         raise FileNotFoundError(f"minicpm5_mk: no config.json in {path}")
-    cfg = from_hf_config(SimpleNamespace(**json.load(open(cfg_path))), max_seq=max_seq)
+    hf = SimpleNamespace(**json.load(open(cfg_path)))
+    _, rope_problem = rope_support(hf)
+    if rope_problem:  # the kernels apply plain RoPE only; scoring with it would be silently wrong
+        raise ValueError(f"minicpm5_mk: {path}: {rope_problem}")
+    cfg = from_hf_config(hf, max_seq=max_seq)
     files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
     if not files:
         raise FileNotFoundError(f"minicpm5_mk: no *.safetensors in {path}")

@@ -95,22 +95,44 @@ def get_config(name: str) -> MkConfig:
     return PRESETS[name]
 
 
+def rope_support(hf) -> tuple:
+    """(rope_theta or None, problem or None) from a HF config's `rope_scaling` / `rope_parameters`
+    (`plugin/minicpm5_mk/model.py:576-585`).  Newer configs keep rope_theta only inside
+    `rope_parameters`; a theta there overrides the top-level field.  Any rope_type other than the
+    plain one ("default", or none given) -- longrope, yarn, linear, dynamic ... -- is a problem: the
+    kernels apply plain RoPE only."""
+    rs = getattr(hf, "rope_scaling", None) or getattr(hf, "rope_parameters", None)
+    if isinstance(rs, dict):
+        rtype = rs.get("rope_type", rs.get("type", "default"))
+        theta = float(rs["rope_theta"]) if rs.get("rope_theta") is not None else None
+        if rtype not in (None, "default"):
+            return theta, f"rope_scaling={rs} unsupported"
+        return theta, None
+    if rs:
+        return None, f"rope_scaling={rs} unsupported"
+    return None, None
+
+
 def from_hf_config(hf, max_seq: int = 8192) -> MkConfig:
     """Config from a HF/vLLM `hf_config` (fields as read by `plugin/minicpm5_mk/model.py:561-567`).
 
     MiniCPM checkpoints carry `scale_emb`, `scale_depth` and `dim_model_base`; plain Llama ones do not,
-    in which case the three scalars stay 1.0."""
+    in which case the three scalars stay 1.0.  rope_theta comes from `rope_parameters` / `rope_scaling`
+    when they hold one (`rope_support`); whether the rope type is supported is for the caller to check."""
     L = int(hf.num_hidden_layers)
     H = int(hf.hidden_size)
     n_q = int(hf.num_attention_heads)
     hd = int(getattr(hf, "head_dim", None) or H // n_q)
+    theta, _ = rope_support(hf)
+    if theta is None:
+        theta = float(getattr(hf, "rope_theta", 10000.0) or 10000.0)
     scale_emb = float(getattr(hf, "scale_emb", 1.0) or 1.0)
     scale_depth = getattr(hf, "scale_depth", None)
     dim_base = getattr(hf, "dim_model_base", None)
     return MkConfig(
         num_layers=L, hidden=H, inter=int(hf.intermediate_size), n_q=n_q,
         n_kv=int(getattr(hf, "num_key_value_heads", n_q)), head_dim=hd, vocab=int(hf.vocab_size),
-        rope_theta=float(getattr(hf, "rope_theta", 10000.0) or 10000.0), eps=float(hf.rms_norm_eps),
+        rope_theta=theta, eps=float(hf.rms_norm_eps),
         scale_emb=scale_emb,
         residual_scale=(float(scale_depth) / math.sqrt(L)) if scale_depth is not None else 1.0,
         logit_scale=(float(dim_base) / H) if dim_base is not None else 1.0,

@@ -85,14 +85,23 @@ def _slice(buf: torch.Tensor, ptr: int, nbytes: int) -> torch.Tensor:
 
 
 def nccl_allgather(group=None) -> Callable[[torch.Tensor], AllGather]:
-    """All-gather through torch.distributed (NCCL): returns a factory taking the rank's workspace."""
+    """All-gather through torch.distributed (NCCL): returns a factory taking the rank's workspace.
+
+    torch's NCCL collectives order themselves against torch's current stream, so the gather runs with
+    the stream the library passes made current: it then starts after the send rows are written and
+    attention (issued after the callback returns) reads the receive rows only after it."""
     import torch.distributed as dist
 
     def bind(ws: torch.Tensor) -> AllGather:
         world = dist.get_world_size(group)
 
         def gather(send: int, recv: int, nbytes: int, stream: int) -> int:
-            dist.all_gather_into_tensor(_slice(ws, recv, nbytes * world), _slice(ws, send, nbytes), group=group)
+            out, inp = _slice(ws, recv, nbytes * world), _slice(ws, send, nbytes)
+            if ws.is_cuda and stream and stream != torch.cuda.current_stream(ws.device).cuda_stream:
+                with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=ws.device)):
+                    dist.all_gather_into_tensor(out, inp, group=group)
+            else:
+                dist.all_gather_into_tensor(out, inp, group=group)
             return 0
 
         return gather
