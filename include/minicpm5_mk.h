@@ -43,35 +43,40 @@ typedef enum mk_status {
 } mk_status;
 
 /* Model configuration: plugin/minicpm5_mk/model.py:561-567 plus the MiniCPM muP scalars.
- *   x = scale_emb * embed[ids];  x += residual_scale * branch;  logits = logit_scale * h @ lm_head^T */
+ *   x = scale_emb * embed[ids];  x += residual_scale * branch;  logits = logit_scale * h @ lm_head^T
+ * weight_bits: format of the projection weights -- 8 (or 0): int8 weight-only, per-output-channel f32
+ * scales (the reference's `_quantize_w`, plugin/minicpm5_mk/mk_weights.py:113-123); 16: bf16 weights,
+ * unquantised (the scales are then 1.0). */
 typedef struct mk_config {
   int32_t num_layers, hidden, inter, n_q, n_kv, head_dim, vocab, max_seq;
   float eps, rope_theta, scale_emb, residual_scale, logit_scale;
+  int32_t weight_bits;
 } mk_config;
 
 /* Device pointers of the prepared weights (layout written by minicpm5_mk/mk_weights.py):
  *   embed, lm_head : bf16 [vocab, hidden]
  *   final_norm     : f32  [hidden]
  *   rope_cos/sin   : f32  [max_seq, head_dim/2]
- *   w_qkv  int8 [L, (n_q+2 n_kv) head_dim, hidden]   s_qkv  f32 [L, (n_q+2 n_kv) head_dim]
- *   w_o    int8 [L, hidden, n_q head_dim]            s_o    f32 [L, hidden]
- *   w_gu   int8 [L, 2 inter, hidden] (gate/up rows alternating: row 2i gate i, row 2i+1 up i)
- *                                                    s_gu   f32 [L, 2 inter]
- *   w_down int8 [L, hidden, inter]                   s_down f32 [L, hidden]
- * The Q rows carry 1/sqrt(head_dim); RMSNorm gains are folded into the weight columns. */
+ *   w_qkv  W [L, (n_q+2 n_kv) head_dim, hidden]   s_qkv  f32 [L, (n_q+2 n_kv) head_dim]
+ *   w_o    W [L, hidden, n_q head_dim]            s_o    f32 [L, hidden]
+ *   w_gu   W [L, 2 inter, hidden] (gate/up rows alternating: row 2i gate i, row 2i+1 up i)
+ *                                                 s_gu   f32 [L, 2 inter]
+ *   w_down W [L, hidden, inter]                   s_down f32 [L, hidden]
+ * W is int8 or bf16 as mk_config.weight_bits says.  The Q rows carry 1/sqrt(head_dim); RMSNorm gains
+ * are folded into the weight columns. */
 typedef struct mk_weight_ptrs {
   const void* embed;
   const void* lm_head;
   const float* final_norm;
   const float* rope_cos;
   const float* rope_sin;
-  const int8_t* w_qkv;
+  const void* w_qkv;
   const float* s_qkv;
-  const int8_t* w_o;
+  const void* w_o;
   const float* s_o;
-  const int8_t* w_gu;
+  const void* w_gu;
   const float* s_gu;
-  const int8_t* w_down;
+  const void* w_down;
   const float* s_down;
 } mk_weight_ptrs;
 
@@ -196,6 +201,35 @@ typedef enum mk_gemm_mode {
 mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
                         int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
                         float* resid32, int32_t ld_resid32, void* stream);
+
+/* Fused epilogue work of one W8A16 GEMM launch, as the forward's projections use it.  Zero / NULL fields
+ * switch a part off.
+ *   rowsq     f32 [M, rowsq_ld]: per-(token, 128-channel tile) sums of squares of the f32 residual.
+ *             ROWSCALE / SWIGLU with rowsq_np > 0 read them: rstd[m] = 1/sqrt(sum of the first rowsq_np
+ *             entries of row m / norm_dim + eps) replaces row_scale (the fused RMSNorm of `fused_qkv`,
+ *             plugin/minicpm5_mk/mk_mlp.py:161-206, `rms_norm_unit`, mk_jax.py:32-36).
+ *             RESID32 writes them: rowsq[m * rowsq_ld + n / 128] = sum over the tile's 128 channels of the
+ *             updated residual squared (rowsq_ld >= N / 128).
+ *   rope_*    ROWSCALE only: columns [0, rope_cols) are heads of head_dim columns whose rotation pairs
+ *             (i, i + head_dim/2) are stored as adjacent columns (2j, 2j + 1); each pair is rotated by the
+ *             angle of position rope_pos_base + m % rope_seq (tables f32 [*, head_dim/2]) before the bf16
+ *             rounding (RoPE of plugin/minicpm5_mk/mk_attn.py:572-589).  rope_cols % 32 == 0. */
+typedef struct mk_gemm_fusion {
+  float* rowsq;
+  int32_t rowsq_ld, rowsq_np, norm_dim;
+  float eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  int32_t rope_cols, head_dim, rope_seq, rope_pos_base;
+  int32_t weight_bits; /* 8 (or 0): w is int8; 16: w is bf16 [N, K] */
+} mk_gemm_fusion;
+
+/* mk_gemm_w8a16 with the fused epilogue work above (fusion may be NULL: then it is mk_gemm_w8a16;
+ * row_scale may be NULL when rowsq_np > 0). */
+mk_status mk_gemm_w8a16_fused(const void* a, int32_t M, int32_t K, int32_t lda, const void* w,
+                              const float* col_scale, int32_t N, int32_t mode, const float* row_scale,
+                              float resid_scale, void* out, int32_t ldo, float* resid32, int32_t ld_resid32,
+                              const mk_gemm_fusion* fusion, void* stream);
 
 /* Causal GQA prefill attention over bs sequences of length seq.  qkv bf16 [bs*seq, ld_qkv] with
  * Q heads at column q_col, K at k_col, V at v_col (each head head_dim wide); out bf16

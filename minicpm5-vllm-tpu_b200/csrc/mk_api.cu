@@ -27,7 +27,14 @@ __device__ int g_mk_err;
 constexpr int kMaxDevices = 64;
 // Weight-operand TMA box rows (one int8 weight tile per k-step).
 constexpr int kWeightBoxRows = mk::GW;
-constexpr int kLmParts = 296;
+constexpr int kLmParts = 296;                // lm_head CTAs (2 per SM) = argmax partials per row
+constexpr int kLmSmemMax = 100 * 1024;       // lm_head hidden rows in shared memory (2 CTAs per SM)
+
+// lm_head launches for bs rows: up to lm_rows_max(H) rows per launch.
+int lm_launches(int bs, int H) {
+  const int nr = mk::lm_rows_max(H);
+  return (bs + nr - 1) / nr;
+}
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -72,13 +79,18 @@ mk_status device_state(DeviceState** out) {
                     mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU>, mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE>,
                     mk::gemm_w8a16_kernel<MK_GEMM_RESID32>})
       MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(mk::G_SMEM_BYTES)));
+                                   static_cast<int>(mk::gemm_smem_bytes(false))));
+    for (auto fn : {mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE, true>, mk::gemm_w8a16_kernel<MK_GEMM_RESID, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU, true>, mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_RESID32, true>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(mk::gemm_smem_bytes(true))));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::TA_SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::TA_SMEM)));
-    MK_CUDA(cudaFuncSetAttribute(mk::attn_last_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
-    MK_CUDA(cudaFuncSetAttribute(mk::lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    for (auto fn : {mk::lm_head_kernel<1>, mk::lm_head_kernel<2>, mk::lm_head_kernel<4>, mk::lm_head_kernel<8>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLmSmemMax));
     if (!g_encode) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -94,11 +106,55 @@ mk_status device_state(DeviceState** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Token operand: bf16 [rows, ld], box 64 (K) x gemm_nt(rows) (tokens), 128-byte swizzle.
-mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
+// Launch `k` on `st`; with `pdl` the launch carries programmatic stream serialization, so the kernel may
+// begin while the previous kernel of the stream drains (every kernel of the forward calls pdl_wait()
+// before touching memory an earlier kernel uses).
+template <typename... KArgs, typename... Args>
+mk_status launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...) == cudaSuccess ? MK_OK : MK_ERR_CUDA;
+}
+
+// Tokens per GEMM tile for M tokens and N output channels on `sms` SMs.  The persistent GEMM runs
+// ceil(tiles / sms) waves of tiles; a tile of nt tokens costs about nt + 32 token-steps (the weight tile's
+// conversion and the epilogue's fixed work).  At large M every size fills its waves and the largest tile
+// wins; when all tiles fit in one or two waves (the projections of one sequence-parallel rank, an
+// isolated N = 1792 GEMM at M = 8192) smaller tiles finish sooner.  Candidates are multiples of 32: the
+// epilogue works in 32-token chunks, and with 32-aligned tiles no chunk straddles a sequence or zig-zag
+// block boundary, and every position's RoPE angle comes from the same table entry and the same number
+// of angle-addition steps whatever the batch size -- which keeps the forward batch-invariant bit for bit.
+int choose_nt(int M, int N, int sms) {
+  if (M < mk::GT) return mk::gemm_nt(M);
+  const int nc = N / mk::GW;
+  int best = mk::GT;
+  long best_cost = -1;
+  for (int nt = mk::GT; nt >= 128; nt -= 32) {
+    const long tiles = static_cast<long>((M + nt - 1) / nt) * nc;
+    const long cost = ((tiles + sms - 1) / sms) * (nt + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = nt;
+    }
+  }
+  return best;
+}
+
+// Token operand: bf16 [rows, ld], box 64 (K) x nt (tokens per tile), 128-byte swizzle.
+mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld, int nt = 0) {
+  if (nt <= 0) nt = mk::gemm_nt(rows);
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GKB), static_cast<cuuint32_t>(mk::gemm_nt(rows))};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GKB), static_cast<cuuint32_t>(nt)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -106,16 +162,19 @@ mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld) {
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
-// Weight operand: int8 [N, K] (K contiguous), box 128 (K) x box_rows (N), 128-byte swizzle (the
-// converters read one row per thread; the swizzle spreads a quarter-warp's rows over all banks).
-mk_status map_b(CUtensorMap* m, const int8_t* w, int N, int K, int box_rows = mk::GW) {
+// Weight operand [N, K] (K contiguous), 128-byte swizzle (the converters read one row per thread; the
+// swizzle spreads a quarter-warp's rows over all banks).  int8: box 128 (K) x box_rows; bf16
+// (wbf16): box 64 (K) x box_rows, two boxes per 128-K stage.
+mk_status map_b(CUtensorMap* m, const void* w, int N, int K, int box_rows = mk::GW, bool wbf16 = false) {
+  const int es_bytes = wbf16 ? 2 : 1;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(mk::GK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * es_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(wbf16 ? mk::GKB : mk::GK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(m, wbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                        const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MK_OK : MK_ERR_CUDA;
 }
 
@@ -128,6 +187,9 @@ struct GemmFusion {
   const float* rope_sin = nullptr;
   int rope_cols = 0, head_dim = 0, rope_seq = 1, rope_pos_base = 0;
   mk::SpLayout sp;  // sequence-parallel rows (RoPE positions)
+  bool pdl = false;  // launch with programmatic stream serialization (inside the forward)
+  int nt = 0;        // tokens per tile, the token tensor map's box height (0: gemm_nt(M))
+  bool wbf16 = false;  // bf16 weights (the weight tensor map is bf16) instead of int8
 };
 
 mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtensorMap& mb, int M, int N, int K,
@@ -138,7 +200,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.M = M;
   ga.N = N;
   ga.K = K;
-  ga.nt = mk::gemm_nt(M);
+  ga.nt = fu.nt > 0 ? fu.nt : mk::gemm_nt(M);
   ga.mode = mode;
   ga.row_scale = row_scale;
   ga.col_scale = col_scale;
@@ -162,26 +224,23 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.err = d->err;
   const int tiles = ((M + ga.nt - 1) / ga.nt) * (N / mk::GW);
   const int grid = std::max(1, std::min(tiles, d->sm_count));
+  const dim3 g(grid), b(mk::G_THREADS);
+  const bool pdl = fu.pdl;
+  const size_t smem = mk::gemm_smem_bytes(fu.wbf16);
+#define MK_GEMM_CASE(MODE)                                                                          \
+  case MODE:                                                                                        \
+    return fu.wbf16 ? launch_k(mk::gemm_w8a16_kernel<MODE, true>, g, b, smem, st, pdl, ma, mb, ga)  \
+                    : launch_k(mk::gemm_w8a16_kernel<MODE, false>, g, b, smem, st, pdl, ma, mb, ga);
   switch (mode) {
-    case MK_GEMM_ROWSCALE:
-      mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-      break;
-    case MK_GEMM_RESID:
-      mk::gemm_w8a16_kernel<MK_GEMM_RESID><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-      break;
-    case MK_GEMM_SWIGLU:
-      mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-      break;
-    case MK_GEMM_COLSCALE:
-      mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-      break;
-    case MK_GEMM_RESID32:
-      mk::gemm_w8a16_kernel<MK_GEMM_RESID32><<<grid, mk::G_THREADS, mk::G_SMEM_BYTES, st>>>(ma, mb, ga);
-      break;
+    MK_GEMM_CASE(MK_GEMM_ROWSCALE)
+    MK_GEMM_CASE(MK_GEMM_RESID)
+    MK_GEMM_CASE(MK_GEMM_SWIGLU)
+    MK_GEMM_CASE(MK_GEMM_COLSCALE)
+    MK_GEMM_CASE(MK_GEMM_RESID32)
     default:
       return MK_ERR_BAD_ARG;
   }
-  return cuda_status(cudaGetLastError());
+#undef MK_GEMM_CASE
 }
 
 mk_status check_gemm_shape(int M, int N, int K, int mode) {
@@ -216,7 +275,8 @@ int ilog2(int v) {
 // a rank's zig-zag rows and K/V the rank-by-rank all-gather (`sp`).
 mk_status launch_attn_split(const DeviceState* d, const void* q_base, int rows, int ld_q, int q_col, const void* kv_base,
                             int S, int ld_kv, int k_col, int v_col, int bs, int n_q, int n_kv, int hd, float scale_log2,
-                            void* out, int ld_out, cudaStream_t st, const mk::SpLayout& sp = mk::SpLayout()) {
+                            void* out, int ld_out, cudaStream_t st, const mk::SpLayout& sp = mk::SpLayout(),
+                            bool pdl = false) {
   const int G = n_q / n_kv;
   const int qpt = 128 / G;
   if (rows % (2 * qpt) || S % mk::TA_BK) return MK_ERR_BAD_SHAPE;
@@ -238,17 +298,15 @@ mk_status launch_attn_split(const DeviceState* d, const void* q_base, int rows, 
   a.err = d->err;
   dim3 grid(a.nqb, n_kv, bs);
   auto* o = static_cast<__nv_bfloat16*>(out);
-  if (hd == 96)
-    mk::attn_tc_kernel<96><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
-  else
-    mk::attn_tc_kernel<128><<<grid, mk::TA_THREADS, mk::TA_SMEM, st>>>(mq, mkm, mv, o, a);
-  return cuda_status(cudaGetLastError());
+  if (hd == 96) return launch_k(mk::attn_tc_kernel<96>, grid, dim3(mk::TA_THREADS), mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
+  return launch_k(mk::attn_tc_kernel<128>, grid, dim3(mk::TA_THREADS), mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
 }
 
 mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
-                      int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st) {
+                      int q_col, int k_col, int v_col, float scale_log2, void* out, int ld_out, cudaStream_t st,
+                      bool pdl = false) {
   return launch_attn_split(d, qkv, S, ld_qkv, q_col, qkv, S, ld_qkv, k_col, v_col, bs, n_q, n_kv, hd, scale_log2, out,
-                           ld_out, st);
+                           ld_out, st, mk::SpLayout(), pdl);
 }
 
 mk_status check_attn_shape(int bs, int S, int n_q, int n_kv, int hd, int ld_qkv, int q_col, int k_col, int v_col,
@@ -276,6 +334,7 @@ struct mk_handle {
   bool bound = false;
   mk_weight_ptrs w;
   int n_qkv = 0, q_dim = 0, kv_dim = 0;
+  bool wbf16 = false;  // bf16 projection weights (weight_bits 16) instead of int8
   std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_down;  // per layer
   CUtensorMap m_kv_last, m_q_last;
 };
@@ -315,6 +374,7 @@ mk_status mk_create(const mk_config* cfg, int32_t device, mk_handle** out) {
       (2 * c.n_kv * c.head_dim) % 128)
     return MK_ERR_BAD_SHAPE;
   if (c.max_seq > 16384) return MK_ERR_BAD_SHAPE;
+  if (c.weight_bits != 0 && c.weight_bits != 8 && c.weight_bits != 16) return MK_ERR_BAD_ARG;
   MK_CUDA(cudaSetDevice(device));
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
@@ -323,6 +383,7 @@ mk_status mk_create(const mk_config* cfg, int32_t device, mk_handle** out) {
   h->device = device;
   h->dev = d;
   h->n_qkv = n_qkv;
+  h->wbf16 = c.weight_bits == 16;
   h->q_dim = c.n_q * c.head_dim;
   h->kv_dim = c.n_kv * c.head_dim;
   *out = h;
@@ -344,15 +405,18 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
   h->m_o.resize(L);
   h->m_gu.resize(L);
   h->m_down.resize(L);
+  const bool wb = h->wbf16;
+  const size_t es = wb ? 2 : 1;  // bytes per weight
+  auto at = [es](const void* base, size_t elems) { return static_cast<const uint8_t*>(base) + elems * es; };
   for (int l = 0; l < L; ++l) {
-    MK_TRY(map_b(&h->m_qkv[l], w->w_qkv + static_cast<size_t>(l) * h->n_qkv * H, h->n_qkv, H, kWeightBoxRows));
-    MK_TRY(map_b(&h->m_o[l], w->w_o + static_cast<size_t>(l) * H * h->q_dim, H, h->q_dim, kWeightBoxRows));
-    MK_TRY(map_b(&h->m_gu[l], w->w_gu + static_cast<size_t>(l) * 2 * I * H, 2 * I, H, kWeightBoxRows));
-    MK_TRY(map_b(&h->m_down[l], w->w_down + static_cast<size_t>(l) * H * I, H, I, kWeightBoxRows));
+    MK_TRY(map_b(&h->m_qkv[l], at(w->w_qkv, static_cast<size_t>(l) * h->n_qkv * H), h->n_qkv, H, kWeightBoxRows, wb));
+    MK_TRY(map_b(&h->m_o[l], at(w->w_o, static_cast<size_t>(l) * H * h->q_dim), H, h->q_dim, kWeightBoxRows, wb));
+    MK_TRY(map_b(&h->m_gu[l], at(w->w_gu, static_cast<size_t>(l) * 2 * I * H), 2 * I, H, kWeightBoxRows, wb));
+    MK_TRY(map_b(&h->m_down[l], at(w->w_down, static_cast<size_t>(l) * H * I), H, I, kWeightBoxRows, wb));
   }
-  const int8_t* wl = w->w_qkv + static_cast<size_t>(L - 1) * h->n_qkv * H;
-  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H, kWeightBoxRows));
-  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H, 2 * h->kv_dim, H, kWeightBoxRows));
+  const uint8_t* wl = at(w->w_qkv, static_cast<size_t>(L - 1) * h->n_qkv * H);
+  MK_TRY(map_b(&h->m_q_last, wl, h->q_dim, H, kWeightBoxRows, wb));
+  MK_TRY(map_b(&h->m_kv_last, wl + static_cast<size_t>(h->q_dim) * H * es, 2 * h->kv_dim, H, kWeightBoxRows, wb));
   h->w = *w;
   h->bound = true;
   return MK_OK;
@@ -360,7 +424,7 @@ mk_status mk_bind_weights(mk_handle* h, const mk_weight_ptrs* w) {
 
 namespace {
 struct Workspace {
-  size_t x32, xb, qkv, attn, hbuf, rowsq, xl32, xlb, ql, al, hl, rowsql, hf, logits, pval, pidx, top1, total;
+  size_t x32, xb, qkv, attn, hbuf, rowsq, xl32, xlb, ql, al, alpart, hl, rowsql, hf, logits, pval, pidx, top1, total;
 };
 
 Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
@@ -383,6 +447,7 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
   w.xlb = take(static_cast<size_t>(bs) * c.hidden * 2);
   w.ql = take(static_cast<size_t>(bs) * h->q_dim * 2);
   w.al = take(static_cast<size_t>(bs) * h->q_dim * 2);
+  w.alpart = take(static_cast<size_t>(bs) * c.n_q * ((seq + mk::AL_KEYS - 1) / mk::AL_KEYS) * (c.head_dim + 2) * 4);
   w.hl = take(static_cast<size_t>(bs) * c.inter * 2);
   w.rowsql = take(static_cast<size_t>(bs) * (c.hidden / 128) * 4);
   w.hf = take(static_cast<size_t>(bs) * c.hidden * 4);
@@ -395,16 +460,21 @@ Workspace plan_workspace(const mk_handle* h, int bs, int seq) {
 }
 
 mk_status lm_head_launch(const DeviceState*, const float* hf, int bs, int H, const void* lm, int V, float* logits,
-                         float* pval, int* pidx, int32_t* top1, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(mk::LM_ROWS) * H * 4;
-  if (smem > 96 * 1024) return MK_ERR_BAD_SHAPE;
-  for (int r0 = 0; r0 < bs; r0 += mk::LM_ROWS) {
-    mk::lm_head_kernel<<<kLmParts, mk::LM_THREADS, smem, st>>>(hf, static_cast<const __nv_bfloat16*>(lm), logits,
-                                                               pval, pidx, bs, H, V, r0);
-    MK_CUDA(cudaGetLastError());
+                         float* pval, int* pidx, int32_t* top1, cudaStream_t st, bool pdl = false) {
+  const int nr_max = mk::lm_rows_max(H);
+  if (static_cast<size_t>(nr_max) * H * 4 > static_cast<size_t>(kLmSmemMax)) return MK_ERR_BAD_SHAPE;
+  if (static_cast<int64_t>(V) * H >= (int64_t{1} << 31)) return MK_ERR_BAD_SHAPE;  // 32-bit row offsets
+  const auto* W = static_cast<const __nv_bfloat16*>(lm);
+  for (int r0 = 0; r0 < bs; r0 += nr_max) {
+    const int left = std::min(nr_max, bs - r0);
+    const int nr = left <= 1 ? 1 : left <= 2 ? 2 : left <= 4 ? 4 : 8;  // rows this launch holds
+    const size_t smem = static_cast<size_t>(nr) * H * 4;
+    auto k = nr == 1 ? mk::lm_head_kernel<1> : nr == 2 ? mk::lm_head_kernel<2> : nr == 4 ? mk::lm_head_kernel<4>
+                                                                                  : mk::lm_head_kernel<8>;
+    MK_TRY(launch_k(k, dim3(kLmParts), dim3(mk::LM_THREADS), smem, st, pdl, hf, W, logits, pval, pidx, bs, H, V, r0));
   }
-  mk::argmax_reduce_kernel<<<bs, 32, 0, st>>>(pval, pidx, kLmParts, top1);
-  return cuda_status(cudaGetLastError());
+  return launch_k(mk::argmax_reduce_kernel, dim3(bs), dim3(32), 0, st, pdl, static_cast<const float*>(pval),
+                  static_cast<const int*>(pidx), static_cast<int>(kLmParts), top1);
 }
 }  // namespace
 
@@ -490,13 +560,23 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
   int32_t* top1 = d_top1 ? d_top1 : reinterpret_cast<int32_t*>(base + ws.top1);
   const float r = c.residual_scale;
 
-  CUtensorMap mx, mattn, mh, mxl, mal, mhl;
-  MK_TRY(map_a(&mx, xb, T, H, H));
-  MK_TRY(map_a(&mattn, attn, T, qd, qd));
-  MK_TRY(map_a(&mh, hb, T, I, I));
+  // token tiles sized per projection (choose_nt); one token tensor map per (buffer, tile size)
+  const int sms = d->sm_count;
+  const int nt_qkv = choose_nt(T, nqkv, sms), nt_o = choose_nt(T, H, sms), nt_gu = choose_nt(T, 2 * I, sms);
+  const int nt_down = nt_o, nt_kv = choose_nt(T, 2 * kvd, sms);
+  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mal, mhl;
+  MK_TRY(map_a(&mx_qkv, xb, T, H, H, nt_qkv));
+  MK_TRY(map_a(&mx_gu, xb, T, H, H, nt_gu));
+  MK_TRY(map_a(&mx_kv, xb, T, H, H, nt_kv));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd, nt_o));
+  MK_TRY(map_a(&mh, hb, T, I, I, nt_down));
   MK_TRY(map_a(&mxl, xlb, bs, H, H));
   MK_TRY(map_a(&mal, al, bs, qd, qd));
   MK_TRY(map_a(&mhl, hl, bs, I, I));
+  auto tiles = [](GemmFusion f, int nt) {
+    f.nt = nt;
+    return f;
+  };
 
   const int rows_per_blk = 8;  // warps per 256-thread block, one row each
   const int np = H / 128;       // 128-column tiles of the residual: RMSNorm partial sums per row
@@ -516,6 +596,8 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
     f.rowsq_np = np;
     f.inv_norm_dim = 1.0f / static_cast<float>(H);
     f.eps = c.eps;
+    f.pdl = true;
+    f.wbf16 = h->wbf16;
     return f;
   };
   auto with_rope = [&](GemmFusion f, int cols, int sq, int pos_base) {
@@ -529,26 +611,29 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
   };
   GemmFusion resid_stats;  // residual epilogues write the statistics
   resid_stats.rowsq = rowsq;
+  resid_stats.pdl = true;
+  resid_stats.wbf16 = h->wbf16;
   resid_stats.rowsq_ld = np;
   GemmFusion resid_stats_last = resid_stats;
   resid_stats_last.rowsq = rowsql;
 
   for (int l = 0; l < L - 1; ++l) {
     // QKV projection with RMSNorm and RoPE (Q/K) fused into the epilogue
-    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
+    MK_TRY(launch_gemm(d, mx_qkv, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
                        h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st, nullptr, 0,
-                       with_rope(norm_from(rowsq), qd + kvd, seq, 0)));
+                       tiles(with_rope(norm_from(rowsq), qd + kvd, seq, 0), nt_qkv)));
     MK_TRY(mark(MK_STAGE_QKV, 1));
-    MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st));
+    MK_TRY(launch_attn(d, qkv, bs, seq, c.n_q, c.n_kv, hd, nqkv, 0, qd, qd + kvd, kLog2e, attn, qd, st, true));
     MK_TRY(mark(MK_STAGE_ATTN, 1));
     MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
-                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, tiles(resid_stats, nt_o)));
     MK_TRY(mark(MK_STAGE_O, 1));
-    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
-                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0, norm_from(rowsq)));
+    MK_TRY(launch_gemm(d, mx_gu, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0,
+                       tiles(norm_from(rowsq), nt_gu)));
     MK_TRY(mark(MK_STAGE_GATE_UP, 1));
     MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, tiles(resid_stats, nt_down)));
     MK_TRY(mark(MK_STAGE_DOWN, 1));
   }
 
@@ -558,10 +643,10 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
     const int l = L - 1;
     const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
     __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
-    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
-                       nullptr, 0, with_rope(norm_from(rowsq), kvd, seq, 0)));
-    mk::gather_last_kernel<<<bs, 256, 0, st>>>(x32, xl32, xlb, bs, seq, H, rowsq, rowsql, np);
-    MK_CUDA(cudaGetLastError());
+    MK_TRY(launch_gemm(d, mx_kv, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
+                       nullptr, 0, tiles(with_rope(norm_from(rowsq), kvd, seq, 0), nt_kv)));
+    MK_TRY(launch_k(mk::gather_last_kernel, dim3(bs), dim3(256), 0, st, true, x32, xl32, xlb, bs, seq, H, rowsq, rowsql,
+                    np));
     MK_TRY(launch_gemm(d, mxl, h->m_q_last, bs, qd, H, MK_GEMM_ROWSCALE, nullptr, sq, ql, qd, 0.f, st, nullptr, 0,
                        with_rope(norm_from(rowsql), qd, 1, seq - 1)));
     AttnLastArgs la;
@@ -575,25 +660,25 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
     la.v_col = kvd;
     la.ld_out = qd;
     la.scale_log2 = kLog2e;
-    const size_t smem = static_cast<size_t>(seq) * 4;
-    if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
-    mk::attn_last_kernel<<<dim3(c.n_q, bs), 256, smem, st>>>(ql, kv, al, la);
-    MK_CUDA(cudaGetLastError());
+    la.nblk = (seq + mk::AL_KEYS - 1) / mk::AL_KEYS;
+    la.part = f32(ws.alpart);
+    MK_TRY(launch_k(mk::attn_last_block_kernel, dim3(la.nblk, c.n_kv, bs), dim3(mk::AL_KEYS), 0, st, true,
+                    static_cast<const __nv_bfloat16*>(ql), static_cast<const __nv_bfloat16*>(kv), la));
+    MK_TRY(launch_k(mk::attn_last_combine_kernel, dim3(c.n_q, bs), dim3(mk::AL_HDMAX), 0, st, true, al, la));
     MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
     MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
-    MK_TRY(mark(MK_STAGE_LAST_LAYER, 7));
+    MK_TRY(mark(MK_STAGE_LAST_LAYER, 8));
   }
 
-  mk::final_norm_kernel<<<bs, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H,
-                                            c.eps, c.logit_scale);
-  MK_CUDA(cudaGetLastError());
+  MK_TRY(launch_k(mk::final_norm_kernel, dim3(bs), dim3(256), 0, st, true, xl32, h->w.final_norm, hf,
+                  static_cast<__nv_bfloat16*>(d_hidden), H, c.eps, c.logit_scale));
   MK_TRY(lm_head_launch(d, hf, bs, H, h->w.lm_head, c.vocab, logits, f32(ws.pval),
-                        reinterpret_cast<int*>(base + ws.pidx), top1, st));
-  return mark(MK_STAGE_HEAD, 1 + (bs + mk::LM_ROWS - 1) / mk::LM_ROWS + 1);
+                        reinterpret_cast<int*>(base + ws.pidx), top1, st, true));
+  return mark(MK_STAGE_HEAD, 1 + lm_launches(bs, H) + 1);
 }
 }  // namespace
 
@@ -628,7 +713,7 @@ int sp_block(const mk_config& c, int seq, int world) {
 
 struct SpWorkspace {
   Workspace local;  // the single-sequence workspace of a rank's seq / world rows
-  size_t kv_send, kv_all, total;
+  size_t kv_send, kv_all, alpart, total;  // alpart: last-position attention partials over all seq keys
 };
 
 SpWorkspace plan_workspace_sp(const mk_handle* h, int seq, int world) {
@@ -638,7 +723,9 @@ SpWorkspace plan_workspace_sp(const mk_handle* h, int seq, int world) {
   const size_t kv_row = static_cast<size_t>(2 * h->kv_dim) * 2;
   w.kv_send = w.local.total;
   w.kv_all = align256(w.kv_send + T * kv_row);
-  w.total = align256(w.kv_all + static_cast<size_t>(seq) * kv_row);
+  w.alpart = align256(w.kv_all + static_cast<size_t>(seq) * kv_row);
+  w.total = align256(w.alpart + static_cast<size_t>(h->cfg.n_q) * ((seq + mk::AL_KEYS - 1) / mk::AL_KEYS) *
+                                    (h->cfg.head_dim + 2) * 4);
   return w;
 }
 
@@ -682,13 +769,22 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
   const float r = c.residual_scale;
   const size_t kv_row_bytes = static_cast<size_t>(2 * kvd) * 2;
 
-  CUtensorMap mx, mattn, mh, mxl, mal, mhl;
-  MK_TRY(map_a(&mx, xb, T, H, H));
-  MK_TRY(map_a(&mattn, attn, T, qd, qd));
-  MK_TRY(map_a(&mh, hb, T, I, I));
+  const int sms = d->sm_count;
+  const int nt_qkv = choose_nt(T, nqkv, sms), nt_o = choose_nt(T, H, sms), nt_gu = choose_nt(T, 2 * I, sms);
+  const int nt_down = nt_o, nt_kv = choose_nt(T, 2 * kvd, sms);
+  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mal, mhl;
+  MK_TRY(map_a(&mx_qkv, xb, T, H, H, nt_qkv));
+  MK_TRY(map_a(&mx_gu, xb, T, H, H, nt_gu));
+  MK_TRY(map_a(&mx_kv, xb, T, H, H, nt_kv));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd, nt_o));
+  MK_TRY(map_a(&mh, hb, T, I, I, nt_down));
   MK_TRY(map_a(&mxl, xlb, 1, H, H));
   MK_TRY(map_a(&mal, al, 1, qd, qd));
   MK_TRY(map_a(&mhl, hl, 1, I, I));
+  auto tiles = [](GemmFusion f, int nt) {
+    f.nt = nt;
+    return f;
+  };
 
   auto mark = [&](int stage, int launches) { return clk ? clk->mark(stage, launches) : MK_OK; };
   if (clk) MK_TRY(clk->start(st));
@@ -707,6 +803,8 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
     f.rowsq_np = np;
     f.inv_norm_dim = 1.0f / static_cast<float>(H);
     f.eps = c.eps;
+    f.pdl = true;
+    f.wbf16 = h->wbf16;
     return f;
   };
   // RoPE at the zig-zag positions of this rank's rows
@@ -722,6 +820,8 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
   };
   GemmFusion resid_stats;
   resid_stats.rowsq = rowsq;
+  resid_stats.pdl = true;
+  resid_stats.wbf16 = h->wbf16;
   resid_stats.rowsq_ld = np;
   GemmFusion resid_stats_last = resid_stats;
   resid_stats_last.rowsq = rowsql;
@@ -734,23 +834,24 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
   };
 
   for (int l = 0; l < L - 1; ++l) {
-    MK_TRY(launch_gemm(d, mx, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
+    MK_TRY(launch_gemm(d, mx_qkv, h->m_qkv[l], T, nqkv, H, MK_GEMM_ROWSCALE, nullptr,
                        h->w.s_qkv + static_cast<size_t>(l) * nqkv, qkv, nqkv, 0.f, st, nullptr, 0,
-                       with_rope_sp(norm_from(rowsq), qd + kvd)));
+                       tiles(with_rope_sp(norm_from(rowsq), qd + kvd), nt_qkv)));
     MK_TRY(mark(MK_STAGE_QKV, 1));
     MK_TRY(gather_kv(qkv + qd, nqkv));
     MK_TRY(mark(MK_STAGE_KV_GATHER, 0));
     MK_TRY(launch_attn_split(d, qkv, T, nqkv, 0, kv_all, seq, 2 * kvd, 0, kvd, 1, c.n_q, c.n_kv, hd, kLog2e, attn, qd,
-                             st, sp));
+                             st, sp, true));
     MK_TRY(mark(MK_STAGE_ATTN, 1));
     MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
-                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+                       h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, tiles(resid_stats, nt_o)));
     MK_TRY(mark(MK_STAGE_O, 1));
-    MK_TRY(launch_gemm(d, mx, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
-                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0, norm_from(rowsq)));
+    MK_TRY(launch_gemm(d, mx_gu, h->m_gu[l], T, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+                       h->w.s_gu + static_cast<size_t>(l) * 2 * I, hb, I, 0.f, st, nullptr, 0,
+                       tiles(norm_from(rowsq), nt_gu)));
     MK_TRY(mark(MK_STAGE_GATE_UP, 1));
     MK_TRY(launch_gemm(d, mh, h->m_down[l], T, H, I, mk::GEMM_RESID32, nullptr,
-                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, resid_stats));
+                       h->w.s_down + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, tiles(resid_stats, nt_down)));
     MK_TRY(mark(MK_STAGE_DOWN, 1));
   }
 
@@ -760,14 +861,13 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
     const int l = L - 1;
     const float* sq = h->w.s_qkv + static_cast<size_t>(l) * nqkv;
     __nv_bfloat16* kv = qkv;  // [T, 2 kv_dim]
-    MK_TRY(launch_gemm(d, mx, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
-                       nullptr, 0, with_rope_sp(norm_from(rowsq), kvd)));
+    MK_TRY(launch_gemm(d, mx_kv, h->m_kv_last, T, 2 * kvd, H, MK_GEMM_ROWSCALE, nullptr, sq + qd, kv, 2 * kvd, 0.f, st,
+                       nullptr, 0, tiles(with_rope_sp(norm_from(rowsq), kvd), nt_kv)));
     MK_TRY(mark(MK_STAGE_LAST_LAYER, 1));
     MK_TRY(gather_kv(kv, 2 * kvd));
     MK_TRY(mark(MK_STAGE_KV_GATHER, 0));
     if (rank != 0) return MK_OK;
-    mk::gather_last_kernel<<<1, 256, 0, st>>>(x32, xl32, xlb, 1, T, H, rowsq, rowsql, np);
-    MK_CUDA(cudaGetLastError());
+    MK_TRY(launch_k(mk::gather_last_kernel, dim3(1), dim3(256), 0, st, true, x32, xl32, xlb, 1, T, H, rowsq, rowsql, np));
     GemmFusion fq = norm_from(rowsql);
     fq.rope_cos = h->w.rope_cos;
     fq.rope_sin = h->w.rope_sin;
@@ -788,23 +888,23 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
     la.ld_out = qd;
     la.scale_log2 = kLog2e;
     la.sp = sp;
-    const size_t smem = static_cast<size_t>(seq) * 4;
-    if (smem > 64 * 1024) return MK_ERR_BAD_SHAPE;
-    mk::attn_last_kernel<<<dim3(c.n_q, 1), 256, smem, st>>>(ql, kv_all, al, la);
-    MK_CUDA(cudaGetLastError());
+    la.nblk = (seq + mk::AL_KEYS - 1) / mk::AL_KEYS;
+    la.part = f32(sw.alpart);
+    MK_TRY(launch_k(mk::attn_last_block_kernel, dim3(la.nblk, c.n_kv, 1), dim3(mk::AL_KEYS), 0, st, true,
+                    static_cast<const __nv_bfloat16*>(ql), static_cast<const __nv_bfloat16*>(kv_all), la));
+    MK_TRY(launch_k(mk::attn_last_combine_kernel, dim3(c.n_q, 1), dim3(mk::AL_HDMAX), 0, st, true, al, la));
     MK_TRY(launch_gemm(d, mal, h->m_o[l], 1, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
     MK_TRY(launch_gemm(d, mxl, h->m_gu[l], 1, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], 1, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
-    MK_TRY(mark(MK_STAGE_LAST_LAYER, 6));
+    MK_TRY(mark(MK_STAGE_LAST_LAYER, 7));
   }
-  mk::final_norm_kernel<<<1, 256, 0, st>>>(xl32, h->w.final_norm, hf, static_cast<__nv_bfloat16*>(d_hidden), H, c.eps,
-                                           c.logit_scale);
-  MK_CUDA(cudaGetLastError());
+  MK_TRY(launch_k(mk::final_norm_kernel, dim3(1), dim3(256), 0, st, true, xl32, h->w.final_norm, hf,
+                  static_cast<__nv_bfloat16*>(d_hidden), H, c.eps, c.logit_scale));
   MK_TRY(lm_head_launch(d, hf, 1, H, h->w.lm_head, c.vocab, logits, f32(ws.pval), reinterpret_cast<int*>(base + ws.pidx),
-                        top1, st));
+                        top1, st, true));
   return mark(MK_STAGE_HEAD, 3);
 }
 }  // namespace
@@ -836,8 +936,8 @@ mk_status mk_forward_sp(mk_handle* h, const int32_t* d_ids, int32_t seq, int32_t
 int32_t mk_launches_per_forward(const mk_handle* h, int32_t bs, int32_t seq) {
   if (!h || bs <= 0 || seq <= 0) return 0;
   const int per_layer = 5;  // qkv gemm (+RMSNorm, RoPE), attention, o gemm, gate/up gemm, down gemm
-  const int last_layer = 7; // kv gemm, gather, q gemm, attention, o gemm, gate/up gemm, down gemm
-  return 1 + (h->cfg.num_layers - 1) * per_layer + last_layer + 1 + (bs + mk::LM_ROWS - 1) / mk::LM_ROWS + 1;
+  const int last_layer = 8; // kv gemm, gather, q gemm, attention (blocks + combine), o, gate/up, down gemms
+  return 1 + (h->cfg.num_layers - 1) * per_layer + last_layer + 1 + lm_launches(bs, h->cfg.hidden) + 1;
 }
 
 mk_status mk_get_error(mk_handle* h, int32_t* device_err) {
@@ -856,22 +956,65 @@ mk_status mk_get_error(mk_handle* h, int32_t* device_err) {
 void mk_destroy(mk_handle* h) { delete h; }
 
 // ------------------------------------------------------------------------------ isolated kernels
-mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
-                        int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
-                        float* resid32, int32_t ld_resid32, void* stream) {
+mk_status mk_gemm_w8a16_fused(const void* a, int32_t M, int32_t K, int32_t lda, const void* w,
+                              const float* col_scale, int32_t N, int32_t mode, const float* row_scale,
+                              float resid_scale, void* out, int32_t ldo, float* resid32, int32_t ld_resid32,
+                              const mk_gemm_fusion* fusion, void* stream) {
   if (!a || !w || !col_scale || !out) return MK_ERR_BAD_ARG;
   MK_TRY(check_gemm_shape(M, N, K, mode));
-  if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale) return MK_ERR_BAD_ARG;
+  GemmFusion fu;
+  const bool norm_in = fusion && fusion->rowsq && fusion->rowsq_np > 0 &&
+                       (mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU);
+  if (fusion) {
+    if (fusion->weight_bits != 0 && fusion->weight_bits != 8 && fusion->weight_bits != 16) return MK_ERR_BAD_ARG;
+    fu.wbf16 = fusion->weight_bits == 16;
+    if (fusion->rowsq) {
+      if (reinterpret_cast<uintptr_t>(fusion->rowsq) & 3u) return MK_ERR_BAD_ALIGN;
+      if (norm_in) {
+        if (fusion->rowsq_np > fusion->rowsq_ld || fusion->norm_dim <= 0) return MK_ERR_BAD_SHAPE;
+      } else if (mode == MK_GEMM_RESID32) {
+        if (fusion->rowsq_ld < N / 128) return MK_ERR_BAD_SHAPE;
+      } else {
+        return MK_ERR_BAD_ARG;  // statistics are read by ROWSCALE / SWIGLU and written by RESID32 only
+      }
+      fu.rowsq = fusion->rowsq;
+      fu.rowsq_ld = fusion->rowsq_ld;
+      fu.rowsq_np = norm_in ? fusion->rowsq_np : 0;
+      fu.inv_norm_dim = norm_in ? 1.0f / static_cast<float>(fusion->norm_dim) : 0.f;
+      fu.eps = fusion->eps;
+    }
+    if (fusion->rope_cols > 0) {
+      if (mode != MK_GEMM_ROWSCALE || !fusion->rope_cos || !fusion->rope_sin) return MK_ERR_BAD_ARG;
+      if (fusion->rope_cols % 32 || fusion->rope_cols > N || fusion->head_dim <= 0 || fusion->head_dim % 2 ||
+          fusion->rope_seq <= 0 || fusion->rope_pos_base < 0)
+        return MK_ERR_BAD_SHAPE;
+      fu.rope_cos = fusion->rope_cos;
+      fu.rope_sin = fusion->rope_sin;
+      fu.rope_cols = fusion->rope_cols;
+      fu.head_dim = fusion->head_dim;
+      fu.rope_seq = fusion->rope_seq;
+      fu.rope_pos_base = fusion->rope_pos_base;
+    }
+  }
+  if ((mode == MK_GEMM_ROWSCALE || mode == MK_GEMM_SWIGLU) && !row_scale && !norm_in) return MK_ERR_BAD_ARG;
   if (mode == MK_GEMM_RESID32 && (!resid32 || !aligned16(resid32) || ld_resid32 % 4 || ld_resid32 < N))
     return resid32 ? MK_ERR_BAD_ALIGN : MK_ERR_BAD_ARG;
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
+  fu.nt = choose_nt(M, N, d->sm_count);
   CUtensorMap ma, mb;
-  MK_TRY(map_a(&ma, a, M, K, lda));
-  MK_TRY(map_b(&mb, w, N, K, kWeightBoxRows));
+  MK_TRY(map_a(&ma, a, M, K, lda, fu.nt));
+  MK_TRY(map_b(&mb, w, N, K, kWeightBoxRows, fu.wbf16));
   return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
-                     static_cast<cudaStream_t>(stream), resid32, ld_resid32);
+                     static_cast<cudaStream_t>(stream), resid32, ld_resid32, fu);
+}
+
+mk_status mk_gemm_w8a16(const void* a, int32_t M, int32_t K, int32_t lda, const int8_t* w, const float* col_scale,
+                        int32_t N, int32_t mode, const float* row_scale, float resid_scale, void* out, int32_t ldo,
+                        float* resid32, int32_t ld_resid32, void* stream) {
+  return mk_gemm_w8a16_fused(a, M, K, lda, w, col_scale, N, mode, row_scale, resid_scale, out, ldo, resid32,
+                             ld_resid32, nullptr, stream);
 }
 
 mk_status mk_attention_prefill(const void* qkv, int32_t bs, int32_t seq, int32_t n_q, int32_t n_kv,

@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // Q, K and V come from the previous kernel
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer

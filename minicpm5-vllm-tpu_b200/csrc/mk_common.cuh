@@ -64,6 +64,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ---------------------------------------------------------------------------------- launch overlap
+// Programmatic dependent launch: the forward launches each kernel with programmatic stream serialization,
+// so it may start (barrier set-up, TMEM allocation, descriptor prefetch, loads of the constant weights)
+// while the previous kernel drains.  pdl_wait() blocks the calling thread until every earlier kernel of
+// the stream has completed and its writes are visible; every thread calls it before its first access to
+// memory an earlier kernel writes or reads.  Without the launch attribute it returns at once.
+// pdl_trigger() lets the next kernel's CTAs be scheduled once every CTA of this grid has issued it (or
+// exited); they still wait in pdl_wait() for this grid to finish.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -376,6 +387,22 @@ __device__ __forceinline__ float silu_f(float g) {
   float t;
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
   return 0.5f * g * (1.0f + t);
+}
+
+// v[j] summed over the 32 lanes of the warp; lane l returns the sum of v[l].
+// Butterfly transpose-reduction: 31 shuffles for 32 sums, in a fixed order.
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = up ? v[i] : v[i + off];
+      const float keep = up ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
 }
 
 }  // namespace mk

@@ -76,11 +76,19 @@ constexpr uint32_t G_W_COL0 = 2 * GT;         // weight ring after the two accum
 constexpr uint32_t G_W_COLS = GK / 2;         // 64 columns per weight slot
 static_assert(G_W_COL0 + GW_SLOTS * G_W_COLS <= G_TMEM_COLS, "TMEM budget");
 static_assert(G_XSUB_BYTES % 1024 == 0 && G_Q_BYTES % 1024 == 0, "swizzle atoms stay aligned");
-constexpr uint32_t G_RING_BYTES = GX_SLOTS * G_X_BYTES + GQ_SLOTS * G_Q_BYTES;
 constexpr uint32_t G_RS_FLOATS = 2 * GT;                 // per-token rstd, double-buffered
 constexpr uint32_t G_SS_FLOATS = 2 * 4 * GT;             // per-(lane quarter, token) sums of squares
-constexpr size_t G_SMEM_BYTES = 1024 /*align pad*/ + G_RING_BYTES + 4 * (G_RS_FLOATS + G_SS_FLOATS) + 512;
-static_assert(G_SMEM_BYTES <= 232448, "shared memory budget");
+
+// Weight-tile ring of the two weight formats: int8 (16 KB per 128 x 128 tile, 3 slots) or bf16 (two
+// 128-row x 64-K panels of 16 KB per tile, 2 slots, so the ring still fits shared memory).
+__host__ __device__ constexpr int gq_slots(bool wbf16) { return wbf16 ? 2 : GQ_SLOTS; }
+__host__ __device__ constexpr uint32_t gq_bytes(bool wbf16) { return wbf16 ? 2 * G_Q_BYTES : G_Q_BYTES; }
+__host__ __device__ constexpr size_t gemm_smem_bytes(bool wbf16) {
+  return 1024 /*align pad*/ + GX_SLOTS * G_X_BYTES + gq_slots(wbf16) * gq_bytes(wbf16) +
+         4 * (G_RS_FLOATS + G_SS_FLOATS) + 512;
+}
+constexpr size_t G_SMEM_BYTES = gemm_smem_bytes(false);
+static_assert(gemm_smem_bytes(false) <= 232448 && gemm_smem_bytes(true) <= 232448, "shared memory budget");
 
 // Tokens per tile for M tokens (a multiple of 16, the UMMA N granularity at M = 128).
 __host__ __device__ constexpr int gemm_nt(int M) { return M >= GT ? GT : ((M + 15) / 16) * 16; }
@@ -123,39 +131,27 @@ __device__ __forceinline__ void st_global_b16(__nv_bfloat16* p, float v) {
   *p = b;
 }
 
-// v[j] (j = token of the chunk) summed over the 32 lanes; lane l returns the sum for token l.
-// Butterfly transpose-reduction: 31 shuffles for 32 sums, in a fixed order.
-__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool up = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = up ? v[i] : v[i + off];
-      const float keep = up ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
-
-template <int MODE>
+// WB: the weights are bf16 [N, K] instead of int8 (the same kernel without quantisation: the weight
+// tiles arrive as two 64-K panels and the converter warps copy them into TMEM unchanged).
+template <int MODE, bool WB = false>
 __global__ void __launch_bounds__(G_THREADS, 1)
     gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                       const GemmArgs args) {
+  constexpr int QS = gq_slots(WB);
+  constexpr uint32_t QB = gq_bytes(WB);
   extern __shared__ uint8_t g_smem_raw[];
   const uint32_t raw = smem_u32(g_smem_raw);
   uint8_t* sbase = g_smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sX = sbase;                                     // [GX_SLOTS] token tiles
-  uint8_t* sQ = sX + GX_SLOTS * G_X_BYTES;                 // [GQ_SLOTS] int8 weight tiles
-  float* rs_s = reinterpret_cast<float*>(sQ + GQ_SLOTS * G_Q_BYTES);  // [2][GT]
+  uint8_t* sQ = sX + GX_SLOTS * G_X_BYTES;                 // [QS] weight tiles
+  float* rs_s = reinterpret_cast<float*>(sQ + QS * QB);    // [2][GT]
   float* ss_s = rs_s + G_RS_FLOATS;                                    // [2][4][GT]
   uint64_t* bars = reinterpret_cast<uint64_t*>(ss_s + G_SS_FLOATS);
   uint64_t* x_full = bars;                   // [GX_SLOTS] TMA landed
   uint64_t* x_empty = x_full + GX_SLOTS;     // [GX_SLOTS] MMAs reading the slot finished
-  uint64_t* q_full = x_empty + GX_SLOTS;     // [GQ_SLOTS] TMA landed
-  uint64_t* q_empty = q_full + GQ_SLOTS;     // [GQ_SLOTS] converters read the slot
-  uint64_t* w_full = q_empty + GQ_SLOTS;     // [GW_SLOTS] converters wrote the TMEM weight slot
+  uint64_t* q_full = x_empty + GX_SLOTS;     // [QS] TMA landed
+  uint64_t* q_empty = q_full + QS;           // [QS] converters read the slot
+  uint64_t* w_full = q_empty + QS;           // [GW_SLOTS] converters wrote the TMEM weight slot
   uint64_t* w_empty = w_full + GW_SLOTS;     // [GW_SLOTS] MMAs reading the TMEM slot finished
   uint64_t* tfull = w_empty + GW_SLOTS;      // [2] accumulator ready
   uint64_t* tempty = tfull + 2;              // [2] accumulator drained by the epilogue
@@ -172,7 +168,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       mbar_init(&x_full[s], 1);
       mbar_init(&x_empty[s], 1);
     }
-    for (int s = 0; s < GQ_SLOTS; ++s) {
+    for (int s = 0; s < QS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], G_CONV_WARPS);
     }
@@ -199,6 +195,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
 
   const int nt = args.nt;
   const int num_c = args.N / GW;                 // channel tiles
@@ -217,7 +214,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // 148 CTAs share a few token tiles in L2 at any time.
     const bool leader = elect_one();
     const bool is_x = warp == 0;
-    const int slots = is_x ? GX_SLOTS : GQ_SLOTS;
+    // the token tiles come from the previous kernel; the weights are constant, so their producer (and the
+    // converters and the MMA warp, which touch no global memory) start before the previous kernel ends
+    if (is_x) pdl_wait();
+    const int slots = is_x ? GX_SLOTS : QS;
     uint64_t* full = is_x ? x_full : q_full;
     uint64_t* empty = is_x ? x_empty : q_empty;
     const uint32_t x_panel = static_cast<uint32_t>(nt) * GKB * 2;
@@ -235,9 +235,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           tma_load_2d(sX + s * G_X_BYTES, &tmX, &full[s], kt * GK, (tile / num_c) * nt);
           if (two) tma_load_2d(sX + s * G_X_BYTES + G_XSUB_BYTES, &tmX, &full[s], kt * GK + GKB, (tile / num_c) * nt);
         } else {
-          // one 128 x 128 box; a half last stage reads zeros past K
-          mbar_arrive_expect_tx(&full[s], G_Q_BYTES);
-          tma_load_2d(sQ + s * G_Q_BYTES, &tmW, &full[s], kt * GK, (tile % num_c) * GW);
+          // int8: one 128 x 128 box; bf16: two 128-row x 64-K boxes.  A half last stage reads zeros
+          // past K.
+          mbar_arrive_expect_tx(&full[s], QB);
+          tma_load_2d(sQ + s * QB, &tmW, &full[s], kt * GK, (tile % num_c) * GW);
+          if (WB) tma_load_2d(sQ + s * QB + G_Q_BYTES, &tmW, &full[s], kt * GK + GKB, (tile % num_c) * GW);
         }
       }
       __syncwarp();
@@ -295,6 +297,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int et = (warp - G_EPI_WARP0) * 32 + lane;
     const int ch = q * 32 + lane;            // output channel within the tile (= TMEM lane)
     const float r = args.resid_scale;
+    pdl_wait();  // statistics, residual and outputs are shared with earlier kernels
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = blockIdx.x + it * gridDim.x;
       const int tb = tile / num_c, cb = tile % num_c;
@@ -498,7 +501,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
     }
   } else {
-    // -------------------------------------------------------------------- int8 -> bf16 converters
+    // -------------------------------------------------------------------- int8 -> bf16 converters (bf16: copy)
     // Thread = one weight row (output channel) of the tile, half of the stage's 128 K values.
     // Weight tiles arrive 128B-swizzled: 16-byte chunk c of row rr sits at rr*128 + ((c ^ (rr&7))<<4),
     // so the eight rows of each quarter-warp phase hit distinct banks.
@@ -509,19 +512,34 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const uint32_t xsw = rr & 7;
     const uint32_t toff = static_cast<uint32_t>(cq * 32) << 16;
     for (int idx = 0; idx < total; ++idx) {
-      const int sq = idx % GQ_SLOTS, sw = idx % GW_SLOTS;
-      if (!mbar_wait(&q_full[sq], (idx / GQ_SLOTS) & 1, abort_flag)) break;
-      const uint8_t* rowp = sQ + sq * G_Q_BYTES + rr * GK;
-      uint4 v[CPT];
-#pragma unroll
-      for (int c = 0; c < CPT; ++c) v[c] = *reinterpret_cast<const uint4*>(rowp + (((kh * CPT + c) ^ xsw) << 4));
+      const int sq = idx % QS, sw = idx % GW_SLOTS;
+      if (!mbar_wait(&q_full[sq], (idx / QS) & 1, abort_flag)) break;
       uint32_t o[8 * CPT];
+      if constexpr (WB) {
+        // bf16 weights: this thread's half of the row is panel kh (64 K = eight 16-byte chunks), already
+        // in the TMEM operand's format (two consecutive K per 32-bit word, lower K in the low half)
+        static_assert(CPT == 4, "bf16 weights: one 64-K panel per converter thread");
+        const uint8_t* rowp = sQ + sq * QB + kh * G_Q_BYTES + rr * 128;
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) {
-        i8x4_to_bf16x4(v[c].x, o[8 * c + 0], o[8 * c + 1]);
-        i8x4_to_bf16x4(v[c].y, o[8 * c + 2], o[8 * c + 3]);
-        i8x4_to_bf16x4(v[c].z, o[8 * c + 4], o[8 * c + 5]);
-        i8x4_to_bf16x4(v[c].w, o[8 * c + 6], o[8 * c + 7]);
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((c ^ xsw) << 4));
+          o[4 * c] = v.x;
+          o[4 * c + 1] = v.y;
+          o[4 * c + 2] = v.z;
+          o[4 * c + 3] = v.w;
+        }
+      } else {
+        const uint8_t* rowp = sQ + sq * QB + rr * GK;
+        uint4 v[CPT];
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) v[c] = *reinterpret_cast<const uint4*>(rowp + (((kh * CPT + c) ^ xsw) << 4));
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          i8x4_to_bf16x4(v[c].x, o[8 * c + 0], o[8 * c + 1]);
+          i8x4_to_bf16x4(v[c].y, o[8 * c + 2], o[8 * c + 3]);
+          i8x4_to_bf16x4(v[c].z, o[8 * c + 4], o[8 * c + 5]);
+          i8x4_to_bf16x4(v[c].w, o[8 * c + 6], o[8 * c + 7]);
+        }
       }
       // Every lane has consumed its loaded bytes (the conversion used them), so the TMA may now
       // overwrite the slot.  Releasing it right after issuing the loads let a refill race them.

@@ -14,6 +14,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __nv_bfloat1
                              float* __restrict__ x32, __nv_bfloat16* __restrict__ xb, int T, int H, int V, float scale,
                              int* err, float* __restrict__ rowsq = nullptr, int rowsq_ld = 0,
                              SpLayout sp = SpLayout()) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -107,6 +109,8 @@ __global__ void gather_last_kernel(const float* __restrict__ x32, float* __restr
                                    __nv_bfloat16* __restrict__ xlb, int bs, int S, int H,
                                    const float* __restrict__ rowsq = nullptr, float* __restrict__ rowsql = nullptr,
                                    int rowsq_ld = 0) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const size_t srow = static_cast<size_t>(b) * S + S - 1;
   const float* src = x32 + srow * H;
@@ -125,6 +129,8 @@ __global__ void gather_last_kernel(const float* __restrict__ x32, float* __restr
 // unscaled normed row when requested (the reference op's (bs, H) bf16 output).
 __global__ void final_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ hf,
                                   __nv_bfloat16* __restrict__ hidden, int H, float eps, float logit_scale) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int b = blockIdx.x;
   const float* xr = x + static_cast<size_t>(b) * H;
@@ -150,77 +156,169 @@ __global__ void final_norm_kernel(const float* __restrict__ x, const float* __re
   }
 }
 
-// logits[b, v] = sum_k hf[b, k] * W[v, k] (f32 accumulate, bf16 W [V, H]); per-CTA argmax
-// partials (value, lowest index on ties).  Rows are processed in groups of LM_ROWS so the f32
-// hidden rows fit in shared memory; each warp owns one vocab row at a time.
-constexpr int LM_ROWS = 8;
+// logits[b, v] = sum_k hf[b, k] * W[v, k] (f32 accumulate, bf16 W [V, H]) for up to NR rows per launch,
+// with per-CTA argmax partials (value, lowest index on ties).  HBM-bound: W (225 MB for the 1B vocab) is
+// streamed once per launch for all NR rows.
+//
+// Layout.  Warp = LM_R consecutive vocab rows at a time; lane l reads 16-byte chunks c = l, l + 32, ... of
+// each row (a warp's load of one row is 512 contiguous bytes), so lane l owns the 8 k values of its chunks.
+// The NR hidden rows sit in shared memory as f32 in a chunk-split layout, hs[n][half][c][4] holding
+// hf[n][8c + 4 half + j], so each lane's 4 values of one half are one conflict-free 16-byte load.  Every
+// weight value feeds NR FMAs and every loaded hidden value LM_R of them (two rows per packed f32x2 FMA).
+// At the end of a vocab group the warp sums the LM_R x NR per-lane partials over its lanes (butterfly
+// transpose-reduction) and each sum's owner lane stores the logit and keeps its running argmax.
 constexpr int LM_THREADS = 256;
+constexpr int LM_R = 4;  // vocab rows per warp group
+
+// Rows per launch: 8 (the hidden rows of a launch take 8 * H * 4 bytes of shared memory, two CTAs per SM).
+// At 16 rows the accumulators no longer fit the 128 registers a thread has at two CTAs per SM.
+__host__ __device__ constexpr int lm_rows_max(int H) { return H * 8 * 4 <= 100 * 1024 ? 8 : 4; }
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-__global__ void __launch_bounds__(LM_THREADS)
+// (d0, d1) += (a0, a1) * s in one packed f32x2 FMA.
+__device__ __forceinline__ void fma2_acc(float& d0, float& d1, float a0, float a1, float s) {
+  asm("{\n\t.reg .b64 x, y, z;\n\t"
+      "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\tmov.b64 z, {%0, %1};\n\t"
+      "fma.rn.f32x2 z, x, y, z;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(s));
+}
+
+// 16-byte streaming load of weights that are read once (not kept in L1).
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <int NR>
+__global__ void __launch_bounds__(LM_THREADS, 2)
     lm_head_kernel(const float* __restrict__ hf, const __nv_bfloat16* __restrict__ W, float* __restrict__ logits,
                    float* __restrict__ part_val, int* __restrict__ part_idx, int bs, int H, int V, int row0) {
-  extern __shared__ float lm_smem[];  // [LM_ROWS][H]
-  __shared__ float bval[LM_THREADS / 32][LM_ROWS];
-  __shared__ int bidx[LM_THREADS / 32][LM_ROWS];
-  const int nr = min(LM_ROWS, bs - row0);
-  for (int i = threadIdx.x; i < nr * H; i += blockDim.x) lm_smem[i] = hf[static_cast<size_t>(row0) * H + i];
+  static_assert(NR == 1 || NR == 2 || NR == 4 || NR == 8, "rows per launch");
+  constexpr int NV = LM_R * NR;  // partial sums per vocab group (index i = rr * NR + n)
+  extern __shared__ float lm_smem[];  // [NR][2][H/8][4]
+  __shared__ float bval[LM_THREADS / 32][NR];
+  __shared__ int bidx[LM_THREADS / 32][NR];
+  pdl_wait();
+  pdl_trigger();
+  const int nr = min(NR, bs - row0);
+  const int kc = H / 8;  // 16-byte weight chunks per row
+  for (int i = threadIdx.x; i < NR * H; i += blockDim.x) {
+    const int n = i / H, k = i - n * H;
+    const int c = k >> 3, e = k & 7;
+    lm_smem[static_cast<size_t>(n) * H + (e >> 2) * (H >> 1) + c * 4 + (e & 3)] =
+        n < nr ? hf[static_cast<size_t>(row0 + n) * H + k] : 0.f;
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float best[LM_ROWS];
-  int bi[LM_ROWS];
-#pragma unroll
-  for (int r = 0; r < LM_ROWS; ++r) {
-    best[r] = -INFINITY;
-    bi[r] = 0x7fffffff;
-  }
   const int nwarps = gridDim.x * (LM_THREADS / 32);
-  for (int v = blockIdx.x * (LM_THREADS / 32) + warp; v < V; v += nwarps) {
-    const uint4* wr = reinterpret_cast<const uint4*>(W + static_cast<size_t>(v) * H);
-    float acc[LM_ROWS];
+  const int ngroups = (V + LM_R - 1) / LM_R;
+  float best = -INFINITY;  // for row n = (owned index) % NR
+  int bi = 0x7fffffff;
+  for (int grp = blockIdx.x * (LM_THREADS / 32) + warp; grp < ngroups; grp += nwarps) {
+    const int v0 = grp * LM_R;
+    float acc[LM_R][NR];
 #pragma unroll
-    for (int r = 0; r < LM_ROWS; ++r) acc[r] = 0.f;
-    for (int c = lane; c < H / 8; c += 32) {
-      const uint4 wv = __ldg(wr + c);
-      const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-      float wf[8];
+    for (int rr = 0; rr < LM_R; ++rr)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = unpack_bf16x2(w4[e]);
-        wf[2 * e] = f.x;
-        wf[2 * e + 1] = f.y;
+      for (int n = 0; n < NR; ++n) acc[rr][n] = 0.f;
+    // element offsets of the group's rows (V * H < 2^31 is checked on the host); rows past V repeat the
+    // last one and their sums are dropped
+    int wrow[LM_R];
+#pragma unroll
+    for (int rr = 0; rr < LM_R; ++rr) wrow[rr] = min(v0 + rr, V - 1) * H;
+    // one chunk of every weight row is loaded a step ahead of the one being multiplied
+    uint4 wn[LM_R];
+    if (lane < kc) {
+#pragma unroll
+      for (int rr = 0; rr < LM_R; ++rr) wn[rr] = ldg_stream16(W + wrow[rr] + lane * 8);
+    }
+    for (int c = lane; c < kc; c += 32) {
+      uint4 w[LM_R];
+#pragma unroll
+      for (int rr = 0; rr < LM_R; ++rr) w[rr] = wn[rr];
+      if (c + 32 < kc) {
+#pragma unroll
+        for (int rr = 0; rr < LM_R; ++rr) wn[rr] = ldg_stream16(W + wrow[rr] + (c + 32) * 8);
       }
 #pragma unroll
-      for (int r = 0; r < LM_ROWS; ++r) {
-        if (r < nr) {
-          const float* hr = lm_smem + r * H + c * 8;
+      for (int half = 0; half < 2; ++half) {
+        float wf[LM_R][4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r] += wf[e] * hr[e];
+        for (int rr = 0; rr < LM_R; ++rr) {
+          const uint32_t lo = half ? w[rr].z : w[rr].x, hi = half ? w[rr].w : w[rr].y;
+          const float2 a = unpack_bf16x2(lo), b = unpack_bf16x2(hi);
+          wf[rr][0] = a.x;
+          wf[rr][1] = a.y;
+          wf[rr][2] = b.x;
+          wf[rr][3] = b.y;
+        }
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const float4 hv = *reinterpret_cast<const float4*>(lm_smem + static_cast<size_t>(n) * H + half * (H >> 1) + c * 4);
+          const float h4[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int rr = 0; rr < LM_R; rr += 2) fma2_acc(acc[rr][n], acc[rr + 1][n], wf[rr][j], wf[rr + 1][j], h4[j]);
+          }
         }
       }
     }
+    // sum the partials over the lanes; index i = rr * NR + n
+    float* flat = &acc[0][0];
+    if constexpr (NV >= 32) {
 #pragma unroll
-    for (int r = 0; r < LM_ROWS; ++r) {
-      float t = acc[r];
-      for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
-      if (r < nr) {
-        if (lane == 0) logits[static_cast<size_t>(row0 + r) * V + v] = t;
-        if (better(t, v, best[r], bi[r])) {
-          best[r] = t;
-          bi[r] = v;
+      for (int q = 0; q < NV / 32; ++q) {
+        // in place: the partials are dead after the sum; lane owns index q * 32 + lane
+        const float sum = warp_transpose_sum32(*reinterpret_cast<float(*)[32]>(flat + q * 32), lane);
+        const int i = q * 32 + lane, rr = i / NR, n = i % NR, v = v0 + rr;
+        if (v < V && n < nr) {
+          logits[static_cast<size_t>(row0 + n) * V + v] = sum;
+          if (better(sum, v, best, bi)) {
+            best = sum;
+            bi = v;
+          }
+        }
+      }
+    } else {
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float t = flat[i];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (lane == i) mine = t;
+      }
+      const int rr = lane / NR, n = lane % NR, v = v0 + rr;
+      if (lane < NV && v < V && n < nr) {
+        logits[static_cast<size_t>(row0 + n) * V + v] = mine;
+        if (better(mine, v, best, bi)) {
+          best = mine;
+          bi = v;
         }
       }
     }
   }
-  if (lane == 0) {
+  // lanes l, l ^ NR, l ^ 2NR, ... hold the same row n = l % NR
 #pragma unroll
-    for (int r = 0; r < LM_ROWS; ++r) {
-      bval[warp][r] = best[r];
-      bidx[warp][r] = bi[r];
+  for (int o = 16; o >= NR; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, best, bi)) {
+      best = ov;
+      bi = oi;
     }
+  }
+  if (lane < NR) {
+    bval[warp][lane] = best;
+    bidx[warp][lane] = bi;
   }
   __syncthreads();
   if (threadIdx.x < nr) {
@@ -240,6 +338,8 @@ __global__ void __launch_bounds__(LM_THREADS)
 // top1[b] = argmax over the per-CTA partials of row b (warp-shuffle reduction, ties -> lowest id).
 __global__ void argmax_reduce_kernel(const float* __restrict__ part_val, const int* __restrict__ part_idx,
                                      int nparts, int32_t* __restrict__ top1) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int lane = threadIdx.x;
   float bv = -INFINITY;

@@ -17,6 +17,7 @@ EXPORTED = (
     "mk_get_error", "mk_destroy", "mk_gemm_w8a16", "mk_attention_prefill", "mk_rope", "mk_rms_rstd", "mk_embed",
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward", "mk_lm_head_argmax_noalloc",
     "mk_topk_logprobs", "mk_forward_timed", "mk_sp_block", "mk_workspace_size_sp", "mk_forward_sp",
+    "mk_gemm_w8a16_fused",
 )
 
 MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
@@ -27,12 +28,18 @@ _i32, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p, ctypes.c
 class MkConfigC(ctypes.Structure):
     _fields_ = [("num_layers", _i32), ("hidden", _i32), ("inter", _i32), ("n_q", _i32), ("n_kv", _i32),
                 ("head_dim", _i32), ("vocab", _i32), ("max_seq", _i32), ("eps", _f32), ("rope_theta", _f32),
-                ("scale_emb", _f32), ("residual_scale", _f32), ("logit_scale", _f32)]
+                ("scale_emb", _f32), ("residual_scale", _f32), ("logit_scale", _f32), ("weight_bits", _i32)]
 
 
 class MkWeightPtrsC(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("embed", "lm_head", "final_norm", "rope_cos", "rope_sin", "w_qkv", "s_qkv",
                                    "w_o", "s_o", "w_gu", "s_gu", "w_down", "s_down")]
+
+
+class MkGemmFusionC(ctypes.Structure):
+    _fields_ = [("rowsq", _vp), ("rowsq_ld", _i32), ("rowsq_np", _i32), ("norm_dim", _i32), ("eps", _f32),
+                ("rope_cos", _vp), ("rope_sin", _vp), ("rope_cols", _i32), ("head_dim", _i32), ("rope_seq", _i32),
+                ("rope_pos_base", _i32), ("weight_bits", _i32)]
 
 
 MK_STAGE_NAMES = ("embed", "qkv", "attn", "o_proj", "gate_up", "down", "last_layer", "head", "kv_gather")
@@ -82,6 +89,8 @@ def lib() -> ctypes.CDLL:
         L.mk_destroy.argtypes = [_vp]
         L.mk_gemm_w8a16.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _vp, _i32,
                                     _vp]
+        L.mk_gemm_w8a16_fused.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _vp,
+                                          _i32, ctypes.POINTER(MkGemmFusionC), _vp]
         L.mk_attention_prefill.argtypes = [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp,
                                            _i32, _vp]
         L.mk_rope.argtypes = [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i32, _i32, _vp]

@@ -34,6 +34,8 @@ class MkConfig:
     logit_scale: float = 1.0
     max_seq: int = 8192
     tie_embeddings: bool = False
+    # projection weights: 8 = int8 weight-only per output channel (the BASELINE configs), 16 = bf16
+    weight_bits: int = 8
 
     @property
     def q_dim(self) -> int:
@@ -63,6 +65,8 @@ class MkConfig:
             raise ValueError("hidden % 128, inter % 128, n_q*head_dim % 128 and qkv width % 128 must be 0")
         if (2 * self.n_kv * self.head_dim) % 128:
             raise ValueError("2*n_kv*head_dim must be a multiple of 128")
+        if self.weight_bits not in (8, 16):
+            raise ValueError(f"weight_bits {self.weight_bits} not in (8, 16)")
 
 
 def minicpm_mup(num_layers: int, hidden: int) -> dict:

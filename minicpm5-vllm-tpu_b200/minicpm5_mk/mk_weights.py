@@ -9,6 +9,7 @@ the parts this path keeps, re-laid-out for the tcgen05 GEMMs:
 * int8 weight-only, per-output-channel: scale = max(amax_over_inputs(|W|) / 127, 1e-8),
   q = clamp(round_half_even(W / scale), -127, 127) (`_quantize_w`, `mk_weights.py:113-123`).
   No activation quantisation (the reference's W8A8 SmoothQuant calibration is not used).
+  With `cfg.weight_bits == 16` the same layout is kept in bf16, unquantised, with unit scales.
 * Every projection stays [out_features, in_features] (K contiguous = "K-major" B operand).
 * gate/up are fused into one [2I, H] matrix with alternating rows ([g_0, u_0, g_1, u_1, ...],
   GU_BLOCK = 1): the GEMM keeps one weight row per TMEM lane, so gate and up of a channel sit in
@@ -81,8 +82,16 @@ def pair_heads(w: torch.Tensor, n_heads: int, head_dim: int) -> torch.Tensor:
     return w.reshape(n_heads, head_dim, *w.shape[1:])[:, perm].reshape(w.shape)
 
 
+def quantize_or_cast(w: torch.Tensor, weight_bits: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """int8 per output channel (weight_bits 8) or bf16 with unit scales (weight_bits 16)."""
+    if weight_bits == 16:
+        return w.to(BF16).contiguous(), torch.ones(w.shape[0], dtype=F32, device=w.device)
+    return quantize_per_out_channel(w)
+
+
 def prepare_layer(sd: Dict[str, torch.Tensor], cfg: MkConfig, i: int) -> Dict[str, torch.Tensor]:
     p = f"model.layers.{i}."
+    quant = lambda w: quantize_or_cast(w, cfg.weight_bits)  # noqa: E731
     f = lambda n: sd[p + n].to(F32)  # noqa: E731
     g_in = f("input_layernorm.weight")
     g_post = f("post_attention_layernorm.weight")
@@ -90,15 +99,15 @@ def prepare_layer(sd: Dict[str, torch.Tensor], cfg: MkConfig, i: int) -> Dict[st
     wq = pair_heads(f("self_attn.q_proj.weight") * sm, cfg.n_q, cfg.head_dim)
     wk = pair_heads(f("self_attn.k_proj.weight"), cfg.n_kv, cfg.head_dim)
     wqkv = torch.cat([wq, wk, f("self_attn.v_proj.weight")], 0) * g_in[None, :]
-    w_qkv, s_qkv = quantize_per_out_channel(wqkv)
-    w_o, s_o = quantize_per_out_channel(f("self_attn.o_proj.weight"))
+    w_qkv, s_qkv = quant(wqkv)
+    w_o, s_o = quant(f("self_attn.o_proj.weight"))
     wg = f("mlp.gate_proj.weight") * g_post[None, :]
     wu = f("mlp.up_proj.weight") * g_post[None, :]
-    qg, sg = quantize_per_out_channel(wg)
-    qu, su = quantize_per_out_channel(wu)
+    qg, sg = quant(wg)
+    qu, su = quant(wu)
     w_gu = interleave_gu(qg, qu)
     s_gu = interleave_gu(sg, su)
-    w_down, s_down = quantize_per_out_channel(f("mlp.down_proj.weight"))
+    w_down, s_down = quant(f("mlp.down_proj.weight"))
     return dict(w_qkv=w_qkv, s_qkv=s_qkv, w_o=w_o, s_o=s_o, w_gu=w_gu, s_gu=s_gu, w_down=w_down, s_down=s_down)
 
 

@@ -50,11 +50,16 @@ class MkEngine:
             self.device = torch.device("cuda", torch.cuda.current_device())
         L = _lib.lib()
         c = _lib.MkConfigC(cfg.num_layers, cfg.hidden, cfg.inter, cfg.n_q, cfg.n_kv, cfg.head_dim, cfg.vocab,
-                           cfg.max_seq, cfg.eps, cfg.rope_theta, cfg.scale_emb, cfg.residual_scale, cfg.logit_scale)
+                           cfg.max_seq, cfg.eps, cfg.rope_theta, cfg.scale_emb, cfg.residual_scale, cfg.logit_scale,
+                           cfg.weight_bits)
         h = ctypes.c_void_p()
         _lib.check(L.mk_create(ctypes.byref(c), self.device.index, ctypes.byref(h)), "mk_create")
         self._h = h
         self.weights = {}
+        wdt = torch.bfloat16 if cfg.weight_bits == 16 else torch.int8
+        for k in ("w_qkv", "w_o", "w_gu", "w_down"):
+            if weights[k].dtype != wdt:
+                raise ValueError(f"minicpm5_mk: {k} is {weights[k].dtype}, weight_bits {cfg.weight_bits} wants {wdt}")
         for k in WEIGHT_FIELDS:
             t = weights[k]
             if t.device != self.device:
@@ -188,9 +193,16 @@ class MkEngine:
 # ----------------------------------------------------------------------------------- per-stage ops
 def gemm_w8a16(a: torch.Tensor, w: torch.Tensor, col_scale: torch.Tensor, mode: int,
                row_scale: Optional[torch.Tensor] = None, resid_scale: float = 1.0,
-               out: Optional[torch.Tensor] = None, resid32: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """acc = a @ w^T (a bf16 [M, K], w int8 [N, K]) with the epilogue `mode` (see _lib.MK_GEMM_*).
-    RESID32 updates the f32 residual `resid32` in place and writes its bf16 copy to `out`."""
+               out: Optional[torch.Tensor] = None, resid32: Optional[torch.Tensor] = None, *,
+               rowsq: Optional[torch.Tensor] = None, rowsq_np: int = 0, norm_dim: int = 0, eps: float = 0.0,
+               rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, rope_cols: int = 0, head_dim: int = 0,
+               rope_seq: int = 1, rope_pos_base: int = 0) -> torch.Tensor:
+    """acc = a @ w^T (a bf16 [M, K], w int8 or bf16 [N, K]) with the epilogue `mode` (see _lib.MK_GEMM_*).
+    RESID32 updates the f32 residual `resid32` in place and writes its bf16 copy to `out`.
+
+    The keyword arguments are the forward's fused epilogue work (mk_gemm_w8a16_fused): `rowsq` f32 [M, np]
+    per-(token, 128-channel tile) sums of squares, read into rstd by ROWSCALE / SWIGLU when rowsq_np > 0 and
+    written by RESID32; `rope` = (cos, sin) tables rotating the pair-ordered columns [0, rope_cols)."""
     for t, n in ((a, "a"), (w, "w"), (col_scale, "col_scale")):
         _cuda(t, n)
     M, K = a.shape
@@ -198,11 +210,28 @@ def gemm_w8a16(a: torch.Tensor, w: torch.Tensor, col_scale: torch.Tensor, mode: 
     if out is None:
         width = N // 2 if mode == _lib.MK_GEMM_SWIGLU else N
         out = torch.empty((M, width), dtype=torch.bfloat16, device=a.device)
-    st = _lib.lib().mk_gemm_w8a16(a.data_ptr(), M, K, a.stride(0), w.data_ptr(), col_scale.data_ptr(), N, mode,
-                                  _ptr(row_scale), float(resid_scale), out.data_ptr(), out.stride(0),
-                                  _ptr(resid32), resid32.stride(0) if resid32 is not None else 0,
-                                  _stream(a.device))
-    _lib.check(st, "mk_gemm_w8a16")
+    args = (a.data_ptr(), M, K, a.stride(0), w.data_ptr(), col_scale.data_ptr(), N, mode, _ptr(row_scale),
+            float(resid_scale), out.data_ptr(), out.stride(0), _ptr(resid32),
+            resid32.stride(0) if resid32 is not None else 0)
+    if w.dtype not in (torch.int8, torch.bfloat16):
+        raise ValueError("minicpm5_mk: GEMM weights must be int8 or bf16")
+    if rowsq is None and rope is None and w.dtype == torch.int8:
+        st = _lib.lib().mk_gemm_w8a16(*args, _stream(a.device))
+        _lib.check(st, "mk_gemm_w8a16")
+        return out
+    fu = _lib.MkGemmFusionC()
+    fu.weight_bits = 16 if w.dtype == torch.bfloat16 else 8
+    if rowsq is not None:
+        _cuda(rowsq, "rowsq")
+        fu.rowsq, fu.rowsq_ld, fu.rowsq_np, fu.norm_dim, fu.eps = rowsq.data_ptr(), rowsq.stride(0), rowsq_np, \
+            norm_dim, eps
+    if rope is not None:
+        _cuda(rope[0], "rope_cos")
+        _cuda(rope[1], "rope_sin")
+        fu.rope_cos, fu.rope_sin = rope[0].data_ptr(), rope[1].data_ptr()
+        fu.rope_cols, fu.head_dim, fu.rope_seq, fu.rope_pos_base = rope_cols, head_dim, rope_seq, rope_pos_base
+    st = _lib.lib().mk_gemm_w8a16_fused(*args, ctypes.byref(fu), _stream(a.device))
+    _lib.check(st, "mk_gemm_w8a16_fused")
     return out
 
 

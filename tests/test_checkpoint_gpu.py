@@ -53,3 +53,29 @@ def test_real_checkpoint_passes_reference_gate():
     cand = checkpoint.gate_results(eng, ref["inputs"], k=int(ref.get("k", 20)))
     rep = compare_gate(ref["results"], cand)
     assert rep["gate_v2"] == "PASS", rep
+
+
+@pytest.mark.parametrize("preset,layers,wbits", [("minicpm5-1b", 2, 8), ("minicpm5-2b", 1, 8), ("tiny-hd96", None, 16)])
+def test_device_weight_preparation_matches_cpu(preset, layers, wbits):
+    """prepare_mk_weights on the GPU (what the vLLM class and load_hf_checkpoint(device='cuda') run) gives
+    bit-identical int8 weights and scales to the CPU run whose quantiser is pinned against the reference's
+    `_quantize_w` (plugin/minicpm5_mk/mk_weights.py:113-123; tests/test_oracle.py), and identical bf16
+    weights for weight_bits 16."""
+    import time
+    cfg = PRESETS[preset].replace(weight_bits=wbits)
+    if layers:
+        cfg = cfg.replace(num_layers=layers)
+    sd = random_state_dict(cfg, seed=99)
+    cpu = mk_weights.prepare_mk_weights(sd, cfg)
+    sd_dev = {k: v.to("cuda:0") for k, v in sd.items()}
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dev = mk_weights.prepare_mk_weights(sd_dev, cfg)
+    torch.cuda.synchronize()
+    took = time.perf_counter() - t0
+    assert set(cpu) == set(dev)
+    for k in cpu:
+        assert dev[k].is_cuda, k
+        assert cpu[k].dtype == dev[k].dtype, k
+        assert torch.equal(cpu[k], dev[k].cpu()), k
+    print(f"{preset} x{cfg.num_layers} layers: device preparation {took:.3f} s")

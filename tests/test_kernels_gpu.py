@@ -39,6 +39,7 @@ def _check_err():
 
 GEMM_CASES = [
     # M, K, N
+    (8192, 1536, 1792),  # BASELINE's isolated QKV shape
     (128, 64, 256),
     (256, 128, 384),
     (300, 192, 256),
@@ -87,6 +88,142 @@ def test_gemm_w8a16(dev, M, K, N, mode):
     # bf16 output: almost every element within 1 bf16 ulp of the f32 reference
     rel = ((got - ref).abs() / (ref.abs() + 1e-3)).flatten()
     assert (rel > 1.6e-2).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 1536, 1792), (300, 192, 256), (1000, 4096, 1536), (5, 1536, 1536)])
+@pytest.mark.parametrize("mode", ["rowscale", "resid32", "swiglu"])
+def test_gemm_bf16_weights(dev, M, K, N, mode):
+    """The same GEMM with unquantised bf16 weights (weight_bits 16): the weight tiles are copied into the
+    TMEM operand unchanged, against a plain PyTorch fp32 reference."""
+    from minicpm5_mk import ops, _lib
+    a = _rand((M, K), 101 + M).to(torch.bfloat16)
+    w = _rand((N, K), 102 + N, 0.02).to(torch.bfloat16)
+    s = torch.ones(N)
+    rstd = torch.rand((M,), generator=_gen(103)) + 0.5
+    acc = a.float() @ w.float().T
+    ad, wd, sd, rd = a.to(dev), w.to(dev), s.to(dev), rstd.to(dev)
+    if mode == "rowscale":
+        out = ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_ROWSCALE, row_scale=rd)
+        ref = acc * rstd[:, None]
+    elif mode == "swiglu":
+        out = ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_SWIGLU, row_scale=rd)
+        g, u = acc[:, 0::2] * rstd[:, None], acc[:, 1::2] * rstd[:, None]
+        ref = torch.nn.functional.silu(g) * u
+    else:
+        x0 = _rand((M, N), 104)
+        x32 = x0.to(dev).clone()
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        ops.gemm_w8a16(ad, wd, sd, _lib.MK_GEMM_RESID32, resid_scale=0.3, out=out, resid32=x32)
+        ref = x0 + 0.3 * acc
+        torch.cuda.synchronize()
+        assert (x32.cpu() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item() + 1e-5
+    torch.cuda.synchronize()
+    _check_err()
+    got = out.float().cpu()
+    assert (got - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-3
+
+
+def _rope_pairs_ref(x, cos, sin, rope_cols, hd, pos):
+    """Pair-ordered RoPE: columns (2j, 2j+1) of each head are the rotation pair (j, j + hd/2) at the
+    angle index (column % hd) / 2 of position pos[m]."""
+    out = x.clone()
+    pj = (torch.arange(0, rope_cols, 2) % hd) // 2
+    c, s = cos[pos][:, pj], sin[pos][:, pj]
+    a, b = x[:, 0:rope_cols:2], x[:, 1:rope_cols:2]
+    out[:, 0:rope_cols:2] = a * c - b * s
+    out[:, 1:rope_cols:2] = b * c + a * s
+    return out
+
+
+def _close_bf16(got, ref, what):
+    scale = ref.abs().max().item()
+    err = (got - ref).abs()
+    bad = err > 8e-3 * ref.abs() + 2e-3 * scale
+    assert not bad.any(), (what, err.max().item(), scale, int(bad.sum()))
+
+
+FUSED_CASES = [
+    # M, K, N, head_dim, rope_cols, rope_seq, pos_base: the BASELINE isolated QKV shape (N 1792) with
+    # hd-128 heads; the 1B QKV width (1920, hd 96: Q+K heads rotated, V not) at a ragged M of two
+    # 4096-token sequences plus a tail; positions that wrap inside 32-token chunks (rope_seq 100)
+    (8192, 1536, 1792, 128, 1536, 8192, 0),
+    (8111, 1536, 1920, 96, 1728, 4096, 0),
+    (333, 128, 256, 128, 256, 100, 7),
+]
+
+
+@pytest.mark.parametrize("M,K,N,hd,rope_cols,rope_seq,pos_base", FUSED_CASES)
+def test_gemm_norm_rope_epilogue(dev, M, K, N, hd, rope_cols, rope_seq, pos_base):
+    """The QKV projection's fused epilogue in isolation (mk_gemm_w8a16_fused, ROWSCALE): rstd from the
+    per-(token, 128-channel tile) sums of squares, the per-channel scale, then RoPE on the pair-ordered
+    Q/K columns (positions advanced by the angle-addition recurrence) -- against a plain PyTorch fp32
+    reference on the same inputs."""
+    from minicpm5_mk import ops, _lib
+    from minicpm5_mk.mk_weights import rope_tables
+    a = _rand((M, K), 71 + M).to(torch.bfloat16)
+    w8, s = _quant(_rand((N, K), 72 + N, 0.02))
+    npart = 12
+    rowsq = torch.rand((M, npart), generator=_gen(73)) * 300.0 + 1.0
+    eps = 1e-6
+    rstd = torch.rsqrt(rowsq.sum(-1) / 1536.0 + eps)
+    cos, sin = rope_tables(max(rope_seq + pos_base, 64), hd, 10000.0)
+    acc = (a.float() @ w8.float().T) * rstd[:, None] * s
+    pos = torch.arange(M) % rope_seq + pos_base
+    ref = _rope_pairs_ref(acc, cos, sin, rope_cols, hd, pos)
+    out = ops.gemm_w8a16(a.to(dev), w8.to(dev), s.to(dev), _lib.MK_GEMM_ROWSCALE, rowsq=rowsq.to(dev),
+                         rowsq_np=npart, norm_dim=1536, eps=eps, rope=(cos.to(dev), sin.to(dev)),
+                         rope_cols=rope_cols, head_dim=hd, rope_seq=rope_seq, rope_pos_base=pos_base)
+    torch.cuda.synchronize()
+    _check_err()
+    _close_bf16(out.float().cpu(), ref, "norm+rope")
+
+
+def test_gemm_swiglu_norm_epilogue(dev):
+    """Gate/up with rstd taken from the sums-of-squares partials (the forward's fused post-attention
+    RMSNorm) at a ragged M."""
+    from minicpm5_mk import ops, _lib
+    from minicpm5_mk.mk_weights import interleave_gu
+    M, K, I = 1001, 1536, 4608
+    a = _rand((M, K), 81).to(torch.bfloat16)
+    g8, sg = _quant(_rand((I, K), 82, 0.05))
+    u8, su = _quant(_rand((I, K), 83, 0.05))
+    rowsq = torch.rand((M, 12), generator=_gen(84)) * 200.0 + 1.0
+    rstd = torch.rsqrt(rowsq.sum(-1) / 1536.0 + 1e-6)
+    g = (a.float() @ g8.float().T) * rstd[:, None] * sg
+    u = (a.float() @ u8.float().T) * rstd[:, None] * su
+    ref = torch.nn.functional.silu(g) * u
+    out = ops.gemm_w8a16(a.to(dev), interleave_gu(g8, u8).to(dev), interleave_gu(sg, su).to(dev),
+                         _lib.MK_GEMM_SWIGLU, rowsq=rowsq.to(dev), rowsq_np=12, norm_dim=1536, eps=1e-6)
+    torch.cuda.synchronize()
+    _check_err()
+    got = out.float().cpu()
+    assert (got - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-3
+
+
+@pytest.mark.parametrize("M,K", [(8111, 1536), (8192, 4608)])
+def test_gemm_resid32_writes_norm_statistics(dev, M, K):
+    """o_proj / down (RESID32) update the f32 residual and write each token's sum of squares per
+    128-channel tile -- the statistics the next projection's RMSNorm reads."""
+    from minicpm5_mk import ops, _lib
+    N = 1536
+    a = _rand((M, K), 91 + K).to(torch.bfloat16)
+    w8, s = _quant(_rand((N, K), 92, 0.02))
+    x0 = _rand((M, N), 93)
+    ref = x0 + 0.29 * (a.float() @ w8.float().T) * s
+    x32 = x0.to(dev).clone()
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    rowsq = torch.full((M, 16), -1.0, device=dev)  # 12 tiles written, the rest untouched
+    ops.gemm_w8a16(a.to(dev), w8.to(dev), s.to(dev), _lib.MK_GEMM_RESID32, resid_scale=0.29, out=out,
+                   resid32=x32, rowsq=rowsq)
+    torch.cuda.synchronize()
+    _check_err()
+    x = x32.cpu()
+    assert (x - ref).abs().max().item() <= 1e-4 * ref.abs().max().item() + 1e-5
+    assert torch.equal(out.cpu(), x.to(torch.bfloat16))
+    sq = rowsq.cpu()
+    ref_sq = x.double().pow(2).reshape(M, N // 128, 128).sum(-1)
+    assert torch.allclose(sq[:, :N // 128].double(), ref_sq, rtol=1e-5, atol=1e-4)
+    assert torch.equal(sq[:, N // 128:], torch.full((M, 16 - N // 128), -1.0))
 
 
 @pytest.mark.parametrize("M,K,I", [(256, 128, 128), (777, 384, 512), (4096, 1536, 4608)])
@@ -229,7 +366,8 @@ def test_embed_bad_id_is_reported(dev):
     _check_err()  # cleared
 
 
-@pytest.mark.parametrize("bs,H,V", [(1, 1536, 73448), (3, 384, 1000), (11, 512, 2048)])
+@pytest.mark.parametrize("bs,H,V", [(1, 1536, 73448), (3, 384, 1000), (11, 512, 2048), (32, 1536, 73448),
+                                    (5, 2048, 130560), (2, 1536, 1001)])
 def test_lm_head_argmax(dev, bs, H, V):
     from minicpm5_mk import ops
     h = _rand((bs, H), 51)
