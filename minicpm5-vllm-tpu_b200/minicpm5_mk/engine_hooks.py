@@ -10,6 +10,9 @@ engine patches, plugin/minicpm5_mk/__init__.py:154-244).
   vLLM would split a waiting set of max_tokens=1 requests over several overlapped steps; when they all
   fit into one step they are scheduled as one (so a 32 x 8192 batch is one megakernel call).
 
+* Step marker: GPUModelRunner.execute_model is wrapped so the model's forward knows whether it runs in a
+  real step or in a dummy run (profile, CUDA-graph warm-up / capture); see RUNNER_STEP.
+
 The predicates are plain functions of the request / scheduler fields, unit-tested on CPU; `install`
 wraps the engine classes it is given (vLLM's by default) once.
 """
@@ -26,6 +29,37 @@ ENV_SINGLE_STEP = "TTVLLM_SINGLE_STEP_MT1"
 
 # Whether the engine core of this process serves ARCH (set when an EngineCore is constructed).
 ENGINE_SERVES_ARCH = {"active": False, "logged": False}
+
+# Real scheduler steps in progress in this process (GPUModelRunner.execute_model), and whether the marker
+# is installed.  The model's forward also runs outside real steps -- the profile run, CUDA-graph warm-up
+# and capture -- on dummy batches whose attention metadata can look like any shape; the reference tells
+# them apart the same way, by its runner hook setting the step's batch (plugin/minicpm5_mk/model.py:755-794,
+# reason "dummy").
+RUNNER_STEP = {"depth": 0, "installed": False}
+
+
+def in_runner_step():
+    """True inside a real step, False in a dummy run, None when the marker is not installed."""
+    if not RUNNER_STEP["installed"]:
+        return None
+    return RUNNER_STEP["depth"] > 0
+
+
+def install_step_marker(runner_cls) -> None:
+    if getattr(runner_cls, "_minicpm5_step_marked", False):
+        return
+    orig = runner_cls.execute_model
+
+    def execute_model(self, *args, **kwargs):
+        RUNNER_STEP["depth"] += 1
+        try:
+            return orig(self, *args, **kwargs)
+        finally:
+            RUNNER_STEP["depth"] -= 1
+
+    runner_cls.execute_model = execute_model
+    runner_cls._minicpm5_step_marked = True
+    RUNNER_STEP["installed"] = True
 
 
 def fast_path_length(seq: int) -> bool:
@@ -133,3 +167,9 @@ def install(env=os.environ) -> None:
         install_kv_skip(KVCacheManager, EngineCore)
     if env.get(ENV_SINGLE_STEP, "1") == "1" and hasattr(EngineCore, "step_with_batch_queue"):
         install_single_step(EngineCore)
+    try:
+        from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+    except Exception:  # noqa: BLE001 - no GPU runner in this vLLM: forward falls back to its metadata checks
+        return
+    if hasattr(GPUModelRunner, "execute_model"):
+        install_step_marker(GPUModelRunner)

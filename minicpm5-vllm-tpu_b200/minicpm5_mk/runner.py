@@ -52,3 +52,30 @@ def scatter_last(h: torch.Tensor, bs: int, seq: int, t_pad: int) -> torch.Tensor
     rows = torch.arange(bs, device=h.device) * seq + (seq - 1)
     out[rows] = h
     return out
+
+
+class LastRowScatter:
+    """`scatter_last` into one reused (rows, H) buffer instead of a fresh zero-filled tensor per step
+    (805 MB for a 32 x 8192 step at H 1536).  Each call zeroes only the rows the previous call wrote, then
+    writes this call's last-token rows, so the returned (t_pad, H) view holds zeros everywhere else, as
+    `scatter_last` does.  The buffer grows (once) when a step has more tokens than it holds.  The view
+    stays valid until the next call, which is all vLLM's runner needs: it gathers the sampled rows
+    (`hidden_states[logits_indices]`) before the next forward."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+        self.prev_rows: Optional[torch.Tensor] = None
+
+    def __call__(self, h: torch.Tensor, bs: int, seq: int, t_pad: int) -> torch.Tensor:
+        buf = self.buf
+        if buf is None or buf.shape[0] < t_pad or buf.shape[1] != h.shape[-1] or buf.dtype != h.dtype \
+                or buf.device != h.device:
+            buf = self.buf = None
+            buf = torch.zeros((t_pad, h.shape[-1]), dtype=h.dtype, device=h.device)
+            self.buf, self.prev_rows = buf, None
+        if self.prev_rows is not None:
+            buf.index_fill_(0, self.prev_rows, 0)
+        rows = torch.arange(bs, device=h.device) * seq + (seq - 1)
+        buf.index_copy_(0, rows, h[:bs])
+        self.prev_rows = rows
+        return buf[:t_pad]

@@ -65,3 +65,19 @@ def test_model_class_subclasses_vllm_llama():
     from vllm.model_executor.models.llama import LlamaForCausalLM
     from minicpm5_mk.model import MiniCPM5MegakernelForCausalLM
     assert issubclass(MiniCPM5MegakernelForCausalLM, LlamaForCausalLM)
+
+
+def test_last_row_scatter_reuses_one_buffer():
+    """The reused buffer gives exactly scatter_last's layout step after step (shapes shrinking and
+    growing), zeroing the rows of the previous step."""
+    from minicpm5_mk.runner import LastRowScatter
+    sc = LastRowScatter()
+    g = torch.Generator().manual_seed(0)
+    ptr, cap = None, 0
+    for bs, seq, t_pad in [(2, 4, 10), (3, 2, 8), (1, 8, 8), (2, 4, 9), (4, 4, 20), (1, 4, 4), (2, 8, 16)]:
+        h = torch.randn((bs, 6), generator=g).to(torch.bfloat16)
+        out = sc(h, bs, seq, t_pad)
+        assert torch.equal(out, scatter_last(h, bs, seq, t_pad)), (bs, seq, t_pad)
+        if t_pad <= cap:
+            assert sc.buf.data_ptr() == ptr  # no new allocation while the buffer is large enough
+        ptr, cap = sc.buf.data_ptr(), sc.buf.shape[0]

@@ -85,3 +85,32 @@ def test_installed_hooks_on_fake_engine(monkeypatch):
     Core(other)
     assert not eh.ENGINE_SERVES_ARCH["active"]
     assert Mgr().allocate_slots(_req(), 8192) == "BLOCKS"
+
+
+def test_step_marker_tells_real_steps_from_dummy_runs():
+    """Forward calls inside the runner's execute_model are real steps; the profile run and CUDA-graph
+    warm-up call the model outside it (the reference's "dummy" reason)."""
+    seen = []
+
+    class FakeRunner:
+        def execute_model(self, scheduler_output):
+            seen.append(eh.in_runner_step())
+            return "out"
+
+        def dummy_run(self):
+            seen.append(eh.in_runner_step())
+
+    saved = dict(eh.RUNNER_STEP)
+    try:
+        eh.RUNNER_STEP.update(depth=0, installed=False)
+        assert eh.in_runner_step() is None
+        eh.install_step_marker(FakeRunner)
+        eh.install_step_marker(FakeRunner)  # once only
+        r = FakeRunner()
+        r.dummy_run()
+        assert r.execute_model(None) == "out"
+        r.dummy_run()
+        assert seen == [False, True, False]
+        assert eh.RUNNER_STEP["depth"] == 0
+    finally:
+        eh.RUNNER_STEP.update(saved)
