@@ -50,14 +50,162 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sp", action="store_true", help="skip the sequence-parallel 1 x seq latency (N > 1)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
-    ap.add_argument("--kernel", default=None, choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_kv", "gemm_down", "attn"],
-                    help="time one isolated kernel of the forward (profiling driver) instead of the bench")
+    ap.add_argument("--kernel", default=None,
+                    choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_kv", "gemm_down", "attn", "forward"],
+                    help="time one isolated kernel of the forward, or whole forwards of --kernel-bs sequences "
+                         "(profiling driver), instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
     ap.add_argument("--kernel-iters", type=int, default=3)
     ap.add_argument("--isolated", action="store_true",
                     help="time the isolated-kernel configuration (GEMMs at M=8192, attention at S=8192) and print "
                          "one JSON line per kernel instead of the bench")
+    ap.add_argument("--vllm-e2e", action="store_true",
+                    help="end to end through vLLM: LLM(...) with the reference's engine arguments on a random-init "
+                         "checkpoint of --config, LLM.generate(max_tokens=1, temperature=0) at 1 x seq and "
+                         "--global-bs x seq; prints one JSON line")
+    ap.add_argument("--vllm-child", nargs=2, metavar=("ROLE", "DIR"), default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--vllm-runs", type=int, default=20, help="timed generate calls at 1 x seq (--vllm-e2e)")
+    ap.add_argument("--vllm-runs-batch", type=int, default=5, help="timed generate calls at the global batch")
     return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------ vLLM end to end
+# The reference's headline numbers are LLM.generate end to end (README.md:52-56, benchmark/run_benchmark.py:
+# 368-466) with the engine built as in examples/minimal_vllm_inference.py:90-103.  Each role runs in its own
+# process: `make` writes a random-init checkpoint (bf16 safetensors + config.json), `serve` builds the engine
+# with the reference's arguments and times generate, `direct` computes the same prompts' greedy ids through
+# MkEngine on the same checkpoint (the drop-in must return exactly those).
+VLLM_ENV = {"VLLM_ENABLE_V1_MULTIPROCESSING": "0", "MINICPM5_MK_FREE_STOCK": "1"}
+
+
+def _vllm_prompts(cfg, bs, S, seed):
+    from minicpm5_mk.mk_init import synthetic_ids
+    ids = synthetic_ids(bs, S, seed=seed, vocab=cfg.vocab)
+    ids[:, 0] = 0  # a BOS id first, as the reference's prompts (examples/minimal_vllm_inference.py:115-117)
+    return ids
+
+
+def _vllm_child_make(cfg_name, mdir):
+    from safetensors.torch import save_file
+    from minicpm5_mk.mk_config import get_config
+    from minicpm5_mk.mk_init import param_shapes, make_param
+
+    cfg = get_config(cfg_name)
+    os.makedirs(mdir, exist_ok=True)
+    dev = torch.device("cuda", 0)
+    sd = {n: make_param(n, shp, seed=1234, device=dev).to(torch.bfloat16).cpu().contiguous()
+          for n, shp in param_shapes(cfg).items()}
+    save_file(sd, os.path.join(mdir, "model.safetensors"))
+    hf = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": cfg.hidden,
+          "intermediate_size": cfg.inter, "num_hidden_layers": cfg.num_layers, "num_attention_heads": cfg.n_q,
+          "num_key_value_heads": cfg.n_kv, "head_dim": cfg.head_dim, "vocab_size": cfg.vocab,
+          "max_position_embeddings": 8256, "rms_norm_eps": cfg.eps, "rope_theta": cfg.rope_theta,
+          "tie_word_embeddings": False, "torch_dtype": "bfloat16", "hidden_act": "silu", "bos_token_id": 0,
+          "eos_token_id": 2}
+    if cfg.scale_emb != 1.0 or cfg.residual_scale != 1.0 or cfg.logit_scale != 1.0:
+        # MiniCPM's muP fields (read by minicpm5_mk.mk_config.from_hf_config)
+        import math
+        hf.update(scale_emb=cfg.scale_emb, scale_depth=cfg.residual_scale * math.sqrt(cfg.num_layers),
+                  dim_model_base=cfg.logit_scale * cfg.hidden)
+    with open(os.path.join(mdir, "config.json"), "w") as f:
+        json.dump(hf, f)
+    print(json.dumps({"made": mdir, "params": sum(v.numel() for v in sd.values())}))
+
+
+def _vllm_child_direct(a, mdir):
+    from minicpm5_mk import checkpoint, mk_weights, ops
+    dev = torch.device("cuda", 0)
+    cfg, sd = checkpoint.load_hf_checkpoint(mdir, device=dev, max_seq=8256)
+    eng = ops.MkEngine(cfg, mk_weights.prepare_mk_weights({k: v.float() for k, v in sd.items()}, cfg), dev)
+    del sd
+    out = {}
+    for bs, seed in ((1, 7), (a.global_bs, 8)):
+        ids = _vllm_prompts(cfg, bs, a.seq, seed)
+        _, _, top1 = eng.forward(ids.reshape(-1).contiguous().to(dev), bs, a.seq)
+        out[f"{bs}x{a.seq}"] = top1.cpu().tolist()
+    print(json.dumps({"direct": out}))
+
+
+def _vllm_child_serve(a, mdir):
+    for k, v in VLLM_ENV.items():
+        os.environ.setdefault(k, v)
+    os.environ["MINICPM5_MK_STATUS_DIR"] = os.path.join(mdir, "status")
+    from vllm import LLM, SamplingParams
+    from minicpm5_mk.mk_config import get_config
+
+    cfg = get_config(a.config)
+    t0 = time.perf_counter()
+    # examples/minimal_vllm_inference.py:90-103, minus its TPU compile_sizes (on the GPU runner they ask
+    # inductor for static-shape graphs of the stock model, which the fast path never runs)
+    llm = LLM(model=mdir, skip_tokenizer_init=True, hf_overrides={"architectures": ["MiniCPM5MegakernelForCausalLM"]},
+              tensor_parallel_size=1, dtype="bfloat16", enable_prefix_caching=False, max_model_len=8256,
+              max_num_batched_tokens=262144, max_num_seqs=32, block_size=256, gpu_memory_utilization=0.5)
+    load_s = time.perf_counter() - t0
+    sp = SamplingParams(max_tokens=1, min_tokens=1, temperature=0.0, detokenize=False)
+    res = {"load_s": round(load_s, 1)}
+    for bs, seed, runs, warm in ((1, 7, a.vllm_runs, 5), (a.global_bs, 8, a.vllm_runs_batch, 2)):
+        ids = _vllm_prompts(cfg, bs, a.seq, seed)
+        prompts = [{"prompt_token_ids": ids[b].tolist()} for b in range(bs)]
+        toks = None
+        for _ in range(warm):
+            outs = llm.generate(prompts, sp, use_tqdm=False)
+            toks = [o.outputs[0].token_ids[0] for o in outs]
+        ts = []
+        for _ in range(runs):
+            t = time.perf_counter()
+            outs = llm.generate(prompts, sp, use_tqdm=False)
+            ts.append((time.perf_counter() - t) * 1e3)
+            assert [o.outputs[0].token_ids[0] for o in outs] == toks, "greedy tokens changed between runs"
+        ts.sort()
+
+        def pct(p):
+            k = (len(ts) - 1) * p / 100.0
+            lo = int(k)
+            hi = min(lo + 1, len(ts) - 1)
+            return ts[lo] + (ts[hi] - ts[lo]) * (k - lo)
+
+        res[f"{bs}x{a.seq}"] = {"tokens": toks, "p50_ms": round(pct(50), 3), "p99_ms": round(pct(99), 3),
+                                "runs": runs, "warmup": warm,
+                                "tok_s": round(bs * a.seq / (statistics.mean(ts) / 1e3), 1)}
+    st = os.path.join(mdir, "status", "minicpm5_mk_status_rank0.json")
+    res["status"] = json.load(open(st)) if os.path.exists(st) else None
+    print(json.dumps({"serve": res}))
+
+
+def run_vllm_e2e(a):
+    """LLM.generate end to end at 1 x seq and global_bs x seq (one JSON line), each role in a child."""
+    import tempfile
+    mdir = os.path.join(tempfile.mkdtemp(prefix="mk_vllm_"), a.config)
+
+    def child(role):
+        env = dict(os.environ)
+        env["PYTHONPATH"] = os.pathsep.join([os.path.join(ROOT, "minicpm5-vllm-tpu_b200"), ROOT,
+                                             env.get("PYTHONPATH", "")])
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--config", a.config, "--seq", str(a.seq),
+                            "--global-bs", str(a.global_bs), "--vllm-runs", str(a.vllm_runs),
+                            "--vllm-runs-batch", str(a.vllm_runs_batch), "--vllm-child", role, mdir],
+                           env=env, capture_output=True, text=True, timeout=1800)
+        with open(os.path.join(os.path.dirname(mdir), f"{role}.log"), "w") as f:
+            f.write(r.stdout + "\n" + r.stderr)
+        if r.returncode != 0:
+            err = r.stderr
+            tb = err.rfind("Traceback (most recent call last)")
+            raise RuntimeError(f"vllm child {role} failed (rc {r.returncode}): " + (err[tb:tb + 6000] if tb >= 0
+                                                                                   else err[-4000:]))
+        return json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
+
+    child("make")
+    direct = child("direct")["direct"]
+    serve = child("serve")["serve"]
+    line = {"metric": "vLLM LLM.generate end to end (max_tokens=1, temperature=0)", "config": a.config,
+            "engine_args": "examples/minimal_vllm_inference.py:90-103 without TPU compile_sizes; "
+                           "VLLM_ENABLE_V1_MULTIPROCESSING=0, MINICPM5_MK_FREE_STOCK=1",
+            "load_s": serve["load_s"], "status": serve["status"]}
+    for key in (f"1x{a.seq}", f"{a.global_bs}x{a.seq}"):
+        r = serve[key]
+        line[key] = {k: r[k] for k in ("p50_ms", "p99_ms", "runs", "warmup", "tok_s")}
+        line[key]["tokens_match_direct"] = r["tokens"] == direct[key]
+    print(json.dumps(line), flush=True)
 
 
 def run_kernel(a):
@@ -72,7 +220,17 @@ def run_kernel(a):
     T = a.kernel_bs * a.seq
     g = torch.Generator(device=dev).manual_seed(3)
     H, I = cfg.hidden, cfg.inter
-    if a.kernel.startswith("gemm"):
+    if a.kernel == "forward":
+        from minicpm5_mk import mk_weights
+        from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
+        cfg = cfg.replace(max_seq=max(a.seq, cfg.max_seq))
+        sd = random_state_dict(cfg, seed=1234, device=dev)
+        eng = ops.MkEngine(cfg, mk_weights.prepare_mk_weights(sd, cfg), dev)
+        del sd
+        ids = synthetic_ids(a.kernel_bs, a.seq, seed=1234).reshape(-1).contiguous().to(dev)
+        fn = lambda: eng.forward(ids, a.kernel_bs, a.seq)  # noqa: E731
+        flops = _flops_per_seq(cfg, a.seq) * a.kernel_bs
+    elif a.kernel.startswith("gemm"):
         N, K, mode = {"gemm_swiglu": (2 * I, H, _lib.MK_GEMM_SWIGLU), "gemm_qkv": (cfg.qkv_dim, H, _lib.MK_GEMM_ROWSCALE),
                       "gemm_o": (H, cfg.q_dim, _lib.MK_GEMM_RESID32), "gemm_kv": (2 * cfg.kv_dim, H, _lib.MK_GEMM_ROWSCALE),
                       "gemm_down": (H, I, _lib.MK_GEMM_RESID32)}[a.kernel]
@@ -176,55 +334,98 @@ def _traffic_per_launch(kernel):
     return None
 
 
-def cpu_sample(cfg, S, target_s, threads):
-    """Time the CPU FP32 oracle (restatement of the reference's f32_golden path) on a bounded sample:
-    decoder layers of one S-token sequence run one at a time until ~target_s of CPU time, then
-    extrapolated to the full model.  Returns (tok/s, sample description)."""
-    from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
-    from oracle import golden
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), as the reference's benchmark records it
+    (benchmark/run_benchmark.py:153-167)."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
-    torch.set_num_threads(threads)
-    c1 = cfg.replace(num_layers=1, vocab=min(cfg.vocab, 4096))
-    sd = random_state_dict(c1, seed=1234)
-    W = golden.golden_weights(sd, c1)
-    ids = synthetic_ids(1, S, seed=1234, vocab=c1.vocab)[0]
+
+class CpuLayerSample:
+    """The CPU FP32 oracle (restatement of the reference's f32_golden path) on a bounded sample of the
+    workload: one full decoder layer of one S-token sequence per call (the full model is num_layers such
+    layers plus a last-token lm_head, which is under 0.1 % of the work).  `step()` returns the seconds
+    one layer took; `tok_s(sec)` extrapolates a layer time to the whole model's tokens/s."""
+
+    def __init__(self, cfg, S, threads):
+        from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
+        from oracle import golden
+
+        torch.set_num_threads(threads)
+        self.golden, self.cfg, self.S, self.threads = golden, cfg, S, threads
+        self.c1 = cfg.replace(num_layers=1, vocab=min(cfg.vocab, 4096))
+        self.W = golden.golden_weights(random_state_dict(self.c1, seed=1234), self.c1)
+        self.ids = synthetic_ids(1, S, seed=1234, vocab=self.c1.vocab)[0]
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        self.golden.forward_logits(self.ids, self.W, self.c1, last_only=False)
+        return time.perf_counter() - t0
+
+    def tok_s(self, sec_per_layer: float) -> float:
+        return self.S / (sec_per_layer * self.cfg.num_layers)
+
+    def describe(self, n: int, sec_per_layer: float) -> str:
+        return (f"1 x {self.S} tokens through {n} full decoder layer(s) of the FP32 oracle on {self.threads} "
+                f"threads (median {sec_per_layer:.2f} s/layer); tok/s extrapolated to {self.cfg.num_layers} "
+                f"layers (the last-token lm_head, <0.1% of the work, is left out)")
+
+
+def cpu_sample(cfg, S, target_s, threads):
+    """Time the CPU FP32 oracle on decoder layers of one S-token sequence until ~target_s of CPU time and
+    extrapolate to the full model.  Returns (tok/s, sample description)."""
+    smp = CpuLayerSample(cfg, S, threads)
     times = []
     t_start = time.perf_counter()
     while True:
-        t0 = time.perf_counter()
-        golden.forward_logits(ids, W, c1, last_only=False)
-        times.append(time.perf_counter() - t0)
+        times.append(smp.step())
         if time.perf_counter() - t_start >= target_s or len(times) >= cfg.num_layers:
             break
     per_layer = statistics.median(times)
-    total = per_layer * cfg.num_layers
-    return S / total, (f"1 x {S} tokens through {len(times)} full decoder layer(s) of the FP32 oracle "
-                       f"(median {per_layer:.2f} s/layer), extrapolated x{cfg.num_layers} layers")
+    return smp.tok_s(per_layer), smp.describe(len(times), per_layer)
+
+
+def _workload_config(a, world, bs):
+    return {"workload": f"{a.config} prefill-score {a.global_bs}x{a.seq} (1 greedy token per sequence), "
+                        f"int8 weight-only linears, bf16 activations",
+            "model": a.config, "global_batch": a.global_bs, "seq_len": a.seq, "per_gpu_batch": bs,
+            "parallelism": f"dp{world} (independent full replicas, no collective)",
+            "l2": "working set (0.9 GB weights + activations) larger than L2 every step"}
 
 
 def run_reference(a, rank, world):
     """--impl reference: the reference's CPU FP32 path (oracle port of benchmark/f32_golden.py) on the
-    host cores; rank 0 only."""
+    host cores, rank 0 only.  Each step is a bounded sample of the workload -- one full decoder layer of one
+    8192-token sequence -- and `ms_per_step` is the time those steps took; `value` extrapolates the mean
+    layer time to whole-model tokens/s (the same unit as the GPU arm)."""
     if rank != 0:
         return
     from minicpm5_mk.mk_config import get_config
+    from minicpm5_mk.replicas import shard_bounds
 
     cfg = get_config(a.config)
     threads = os.cpu_count() or 1
-    vals = []
-    desc = ""
-    for i in range(a.warmup + a.steps):
-        v, desc = cpu_sample(cfg, a.seq, target_s=0.0, threads=threads)  # one layer per step
-        if i >= a.warmup:
-            vals.append(v)
-    value = statistics.mean(vals)
+    smp = CpuLayerSample(cfg, a.seq, threads)
+    for _ in range(a.warmup):
+        smp.step()
+    times = [smp.step() for _ in range(a.steps)]
+    sec = statistics.mean(times)
+    value = smp.tok_s(sec)
+    sample = smp.describe(len(times), statistics.median(times))
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": a.gpus,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(a.seq / value * 1e3, 1),
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(sec * 1e3, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{a.config} 1x{a.seq} prefill-score, CPU FP32 oracle (one layer per step, "
-                                   f"extrapolated)", "seq_len": a.seq, "global_batch": 1, "parallelism": "cpu"},
+            "config": _workload_config(a, world, shard_bounds(a.global_bs, world, 0)[1]),
+            "step": f"one decoder layer of one {a.seq}-token sequence (a bounded sample of the workload); value "
+                    f"= {a.seq} tokens / ({cfg.num_layers} x mean step time)",
             "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": desc},
+                             "cpu_model": cpu_model(), "sample": sample},
             "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -289,6 +490,14 @@ def main():
     if a.impl == "reference":
         run_reference(a, rank, world)
         return
+    if a.vllm_child:
+        role, mdir = a.vllm_child
+        {"make": lambda: _vllm_child_make(a.config, mdir), "direct": lambda: _vllm_child_direct(a, mdir),
+         "serve": lambda: _vllm_child_serve(a, mdir)}[role]()
+        return
+    if a.vllm_e2e:
+        run_vllm_e2e(a)
+        return
     if a.kernel:
         run_kernel(a)
         return
@@ -345,6 +554,47 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def all_ranks(vals):
+        """Every rank's list of floats, rank by rank (the same collective on every rank)."""
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world == 1:
+            return [t.tolist()]
+        out = torch.empty((world, len(vals)), dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(out, t)
+        return out.tolist()
+
+    # ---------------------------------------------------------------- latency at 1 x 8192
+    # Measured first, before the throughput loop heats the GPU into its power cap (each of the two figures
+    # is then taken in its own steady state, as the reference times its shapes in separate runs).
+    lat = None
+    if rank == 0 and a.latency_runs > 0:
+        one = ids_dev[0][:S].contiguous()
+        o1 = (hid[:1], lg[:1], top1[:1])
+        for _ in range(5):
+            eng.forward(one, 1, S, out=o1)
+        torch.cuda.synchronize()
+        ts = []
+        lclk = _clock_sampler(local)
+        for _ in range(a.latency_runs):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            eng.forward(one, 1, S, out=o1)
+            s1.record(stream)
+            s1.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        lat_clocks = _clock_summary(lclk)
+        ts.sort()
+
+        def pct(p):
+            k = (len(ts) - 1) * p / 100.0
+            lo = int(k)
+            hi = min(lo + 1, len(ts) - 1)
+            return ts[lo] + (ts[hi] - ts[lo]) * (k - lo)
+
+        lat = {"p50_ms": round(pct(50), 3), "p99_ms": round(pct(99), 3), "runs": len(ts), "warmup": 5,
+               "timing": "device (CUDA events)", "clocks": lat_clocks}
+    barrier()
+
     # ---------------------------------------------------------------- device-timed throughput
     for i in range(a.warmup):
         eng.forward(ids_dev[i], bs, S, out=out)
@@ -363,6 +613,10 @@ def main():
     clocks = _clock_summary(clk)
     dev_ms = ev0.elapsed_time(ev1) / a.steps
     step_ms = max_over_ranks(dev_ms)
+    # every rank's own step time and median SM clock, to name the slowest replica
+    per_rank = [{"rank": r, "ms_per_step": round(v[0], 3), "sequences": int(v[1]),
+                 "sm_mhz": v[2] if v[2] >= 0 else None}
+                for r, v in enumerate(all_ranks([dev_ms, float(bs), float((clocks or {}).get("sm_mhz") or -1)]))]
     err = eng.check_device_error()
     total_tokens = a.global_bs * S
     value = total_tokens / (step_ms / 1e3)
@@ -402,34 +656,6 @@ def main():
         e2e = {"value": round(total_tokens / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(e2e_ms, 3),
                "h2d_bytes_per_step": int(a.global_bs * S * 4), "d2h_bytes_per_step": int(a.global_bs * 4),
                "api": "minicpm5_mk.ops.MkEngine.forward -> mk_forward (C ABI)"}
-
-    # ---------------------------------------------------------------- latency at 1 x 8192
-    lat = None
-    if rank == 0 and a.latency_runs > 0:
-        one = ids_dev[0][:S].contiguous()
-        o1 = (hid[:1], lg[:1], top1[:1])
-        for _ in range(5):
-            eng.forward(one, 1, S, out=o1)
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(a.latency_runs):
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            eng.forward(one, 1, S, out=o1)
-            s1.record(stream)
-            s1.synchronize()
-            ts.append(s0.elapsed_time(s1))
-        ts.sort()
-
-        def pct(p):
-            k = (len(ts) - 1) * p / 100.0
-            lo = int(k)
-            hi = min(lo + 1, len(ts) - 1)
-            return ts[lo] + (ts[hi] - ts[lo]) * (k - lo)
-
-        lat = {"p50_ms": round(pct(50), 3), "p99_ms": round(pct(99), 3), "runs": len(ts), "warmup": 5,
-               "timing": "device (CUDA events)"}
-    barrier()
 
     # ---------------------------------------------------------------- latency at 1 x seq, sequence parallel
     # One sequence over all N ranks (zig-zag blocks, per-layer K/V all-gather over NCCL): every rank runs
@@ -538,24 +764,21 @@ def main():
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, desc = cpu_sample(cfg, S, a.cpu_seconds, threads)
-        cpu = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+        cpu = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+               "sample": desc}
 
     fl_step = _flops_per_seq(cfg, S) * a.global_bs
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{a.config} prefill-score {a.global_bs}x{S} (1 greedy token per sequence), "
-                              f"int8 weight-only linears, bf16 activations",
-                   "model": a.config, "global_batch": a.global_bs, "seq_len": S, "per_gpu_batch": bs,
-                   "parallelism": f"dp{world} (independent full replicas, no collective)",
-                   "l2": "working set (0.9 GB weights + activations) larger than L2 every step"},
+        "config": _workload_config(a, world, bs),
         "model_tflops": round(fl_step / (step_ms / 1e3) / 1e12, 1),
         "model_roofline_frac": round(fl_step / (step_ms / 1e3) / 1e12 / (peak_sus * world), 4),
         "model_roofline_peak": "sustained bf16 GEMM peak per GPU",
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": eng.launches_per_forward(bs, S) * a.steps,
-        "clocks": clocks, "latency_1x8192": lat,
+        "clocks": clocks, "per_rank": per_rank, "latency_1x8192": lat,
         "latency_1x8192_sp": lat_sp, "device_error": err,
     }
     if rank == 0:
