@@ -51,7 +51,8 @@ def _args():
     ap.add_argument("--no-sp", action="store_true", help="skip the sequence-parallel 1 x seq latency (N > 1)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--kernel", default=None,
-                    choices=["gemm_swiglu", "gemm_qkv", "gemm_o", "gemm_kv", "gemm_down", "attn", "forward"],
+                    choices=["gemm_swiglu", "gemm_qkv", "gemm_qkv_rope", "gemm_o", "gemm_kv", "gemm_down", "attn",
+                             "forward", "lm_head"],
                     help="time one isolated kernel of the forward, or whole forwards of --kernel-bs sequences "
                          "(profiling driver), instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
@@ -220,7 +221,14 @@ def run_kernel(a):
     T = a.kernel_bs * a.seq
     g = torch.Generator(device=dev).manual_seed(3)
     H, I = cfg.hidden, cfg.inter
-    if a.kernel == "forward":
+    if a.kernel == "lm_head":
+        # --kernel-bs rows through lm_head + argmax (mk_lm_head_argmax): the vocabulary matrix (225.6 MB at
+        # the 1B config) is streamed once per launch of up to 8 rows
+        W = (torch.randn((cfg.vocab, cfg.hidden), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        hrow = torch.randn((a.kernel_bs, cfg.hidden), generator=g, device=dev)
+        fn = lambda: ops.lm_head_argmax(hrow, W)  # noqa: E731
+        flops = 2.0 * a.kernel_bs * cfg.vocab * cfg.hidden
+    elif a.kernel == "forward":
         from minicpm5_mk import mk_weights
         from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
         cfg = cfg.replace(max_seq=max(a.seq, cfg.max_seq))
@@ -230,6 +238,19 @@ def run_kernel(a):
         ids = synthetic_ids(a.kernel_bs, a.seq, seed=1234).reshape(-1).contiguous().to(dev)
         fn = lambda: eng.forward(ids, a.kernel_bs, a.seq)  # noqa: E731
         flops = _flops_per_seq(cfg, a.seq) * a.kernel_bs
+    elif a.kernel == "gemm_qkv_rope":
+        # the forward's QKV projection: rstd from per-tile sums of squares, RoPE on the Q/K columns
+        from minicpm5_mk.mk_weights import rope_tables
+        N, K = cfg.qkv_dim, H
+        x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
+        w8, s = quantize_per_out_channel(torch.randn((N, K), generator=g, device=dev) * 0.02)
+        rowsq = torch.rand((T, H // 128), generator=g, device=dev) * 128.0 + 1.0
+        cos, sin = (t.to(dev) for t in rope_tables(a.seq, cfg.head_dim, cfg.rope_theta))
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+        fn = lambda: ops.gemm_w8a16(x, w8, s, _lib.MK_GEMM_ROWSCALE, out=out, rowsq=rowsq,  # noqa: E731
+                                    rowsq_np=H // 128, norm_dim=H, eps=cfg.eps, rope=(cos, sin),
+                                    rope_cols=cfg.q_dim + cfg.kv_dim, head_dim=cfg.head_dim, rope_seq=a.seq)
+        flops = 2.0 * T * N * K
     elif a.kernel.startswith("gemm"):
         N, K, mode = {"gemm_swiglu": (2 * I, H, _lib.MK_GEMM_SWIGLU), "gemm_qkv": (cfg.qkv_dim, H, _lib.MK_GEMM_ROWSCALE),
                       "gemm_o": (H, cfg.q_dim, _lib.MK_GEMM_RESID32), "gemm_kv": (2 * cfg.kv_dim, H, _lib.MK_GEMM_ROWSCALE),
@@ -257,7 +278,15 @@ def run_kernel(a):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.kernel_iters
-    print(json.dumps({"kernel": a.kernel, "tokens": T, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1)}))
+    line = {"kernel": a.kernel, "tokens": T, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1)}
+    if a.kernel == "lm_head":
+        line["weight_gbs"] = round(cfg.vocab * cfg.hidden * 2 * -(-a.kernel_bs // 8) / ms / 1e6, 1)
+    if a.kernel == "forward":  # per-stage device time of one more forward (events between the launches)
+        stages = {}
+        eng.forward(ids, a.kernel_bs, a.seq, stage_times=stages)
+        line["stages_ms"] = {k: round(v["ms"], 4) for k, v in stages.items()}
+        line["stages_launches"] = {k: v["launches"] for k, v in stages.items()}
+    print(json.dumps(line))
 
 
 def _peaks():

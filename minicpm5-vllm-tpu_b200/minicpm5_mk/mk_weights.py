@@ -40,10 +40,14 @@ F32 = torch.float32
 
 
 def quantize_per_out_channel(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """w: [out, in] float -> (int8 [out, in], f32 scale [out])."""
+    """w: [out, in] float -> (int8 [out, in], f32 scale [out]).
+
+    The divisor 127 is a tensor, not a Python scalar: torch's CUDA kernels turn division by a scalar into a
+    multiplication by its reciprocal, which can differ from the division in the last bit; tensor / tensor
+    divides exactly on every device, so a GPU preparation matches the CPU one bit for bit."""
     w = w.to(F32)
     amax = w.abs().amax(dim=1, keepdim=True)
-    scale = torch.clamp(amax / 127.0, min=1e-8)
+    scale = torch.clamp(amax / torch.full((), 127.0, dtype=F32, device=w.device), min=1e-8)
     q = torch.clamp(torch.round(w / scale), -127, 127).to(torch.int8)
     return q.contiguous(), scale.squeeze(1).contiguous()
 

@@ -178,8 +178,7 @@ class MiniCPM5MegakernelForCausalLM(LlamaForCausalLM):
                 if getattr(self, "_mk_status", None) is not None:
                     shp = self._mk_status["shapes"].setdefault(key, {"mode": "replica", "steps": 0})
                     shp["steps"] += 1
-                    if shp["steps"] == 1 or self._mk_log_every and shp["steps"] % self._mk_log_every == 0:
-                        self._mk_write_status()
+                    self._mk_write_status()  # only with MINICPM5_MK_STATUS_DIR set: one small file per step
                 ids = input_ids[:bs * seq].to(torch.int32).contiguous()
                 # the registered op (torch.ops.minicpm5_mk.forward -> mk_forward through the C ABI):
                 # final-normed last-token rows, their logits and greedy ids
