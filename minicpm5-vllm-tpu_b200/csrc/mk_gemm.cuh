@@ -126,6 +126,24 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+__device__ __forceinline__ void st_global_b32(__nv_bfloat16* p, uint32_t v) { *reinterpret_cast<uint32_t*>(p) = v; }
+
+// (d0, d1) = (a0, a1) * (b0, b1) and (d0, d1) += (a0, a1) * (b0, b1) as packed f32x2 operations.
+__device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float& d0, float& d1) {
+  asm("{\n\t.reg .b64 x, y, z;\n\t"
+      "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma2(float a0, float a1, float b0, float b1, float& d0, float& d1) {
+  asm("{\n\t.reg .b64 x, y, z;\n\t"
+      "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%0, %1};\n\t"
+      "fma.rn.f32x2 z, x, y, z;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 __device__ __forceinline__ void st_global_b16(__nv_bfloat16* p, float v) {
   const __nv_bfloat16 b = __float2bfloat16_rn(v);
   *p = b;
@@ -363,10 +381,39 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const bool rope = MODE == GEMM_ROWSCALE && cb * GW + q * 32 < args.rope_cols;
       const int pj = rope ? (n % args.head_dim) >> 1 : 0;
       const int hh = args.head_dim >> 1;
+      // RoPE steps of this lane's rotation pair (the table's position-1 and position-2 entries), the sine
+      // carrying the lane's sign: the even lane of a pair computes x_a c - x_b s, the odd one x_b c + x_a s
+      const bool odd_lane = (lane & 1) != 0;
+      const float sg = odd_lane ? 1.f : -1.f;
+      float rct = 1.f, rst = 0.f, rct2 = 1.f, rst2 = 0.f;
+      if (MODE == GEMM_ROWSCALE && rope && args.rope_seq >= 32) {
+        rct = __ldg(args.rope_cos + hh + pj);
+        rst = sg * __ldg(args.rope_sin + hh + pj);
+        rct2 = __ldg(args.rope_cos + 2 * hh + pj);
+        rst2 = sg * __ldg(args.rope_sin + 2 * hh + pj);
+      }
 #pragma unroll 1
       for (int c0 = eh * 32; c0 < nt; c0 += 64) {
         const int tokc = tok0 + c0;
         const int jn = min(min(32, nt - c0), args.M - tokc);  // valid tokens of the chunk (warp-uniform)
+        // RoPE chunk whose 32 tokens have consecutive positions: its four table entries (one per 8
+        // positions) are requested before the accumulator load, so their latency overlaps it
+        int p0 = 0;
+        bool rope_run = false;
+        float tcs[4] = {1.f, 1.f, 1.f, 1.f}, tsn[4] = {0.f, 0.f, 0.f, 0.f};
+        if (MODE == GEMM_ROWSCALE && rope && jn > 0) {
+          // zig-zag blocks are multiples of 32 tokens, so a chunk's positions stay consecutive
+          p0 = args.sp.blk > 0 ? sp_pos(args.sp, tokc) : args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
+          rope_run = args.rope_seq >= 32 && p0 + 32 <= args.rope_seq;
+          if (rope_run) {
+#pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              const size_t e = static_cast<size_t>(p0 + 8 * qd + args.rope_pos_base) * hh + pj;
+              tcs[qd] = __ldg(args.rope_cos + e);
+              tsn[qd] = __ldg(args.rope_sin + e);
+            }
+          }
+        }
         uint32_t acc[32];
         tmem_ld_32x32b_x32(tbase + c0, acc);
         tmem_ld_wait();
@@ -418,30 +465,48 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         } else if (MODE == GEMM_ROWSCALE) {
           __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;
           if (rope) {
-            const bool odd = (lane & 1) != 0;
-            // zig-zag blocks are multiples of 32 tokens, so a chunk's positions stay consecutive
-            const int p0 = args.sp.blk > 0 ? sp_pos(args.sp, tokc) : args.rope_seq >= 32 ? tokc % args.rope_seq : 0;
-            if (args.rope_seq >= 32 && p0 + 32 <= args.rope_seq) {
+            const bool odd = odd_lane;
+            if (rope_run) {
               // The chunk's 32 tokens have consecutive positions: (cos, sin) of the pair's angle at
-              // each position follow from the previous one by the angle-addition rotation with the
-              // one-position step (the table's position-1 entry).  The table is re-read every 8 tokens,
-              // so at most 7 rotations (a few f32 ulps) separate any value from a table entry.
-              const float ct = __ldg(args.rope_cos + hh + pj), st = __ldg(args.rope_sin + hh + pj);
+              // each position follow from a table entry by the angle-addition rotation.  The table is read
+              // every 8 positions (at p, with the one-position step giving p + 1), and the token pairs
+              // (p + 2k, p + 2k + 1) then advance together by the two-position step (the table's position-2
+              // entry), so at most 3 rotations (a few f32 ulps) separate any value from a table entry.
+              // Token pairs also share the packed f32x2 arithmetic, and adjacent lanes swap one result so
+              // that each stores two channels of one token as one 32-bit word.
+              const float ct = rct, st = rst, ct2 = rct2, st2 = rst2;
 #pragma unroll
               for (int hb = 0; hb < 32; hb += 8) {
-                const size_t e = static_cast<size_t>(p0 + hb + args.rope_pos_base) * hh + pj;
-                float c = __ldg(args.rope_cos + e), sn = __ldg(args.rope_sin + e);
+                float cA = tcs[hb >> 3], sA = sg * tsn[hb >> 3];
+                float cB = cA * ct - sA * st, sB = sA * ct + cA * st;
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
+                for (int jj = 0; jj < 8; jj += 2) {
                   const int j = hb + jj;
-                  const float x = __uint_as_float(acc[j]) * rsb[c0 + j] * cs;
-                  const float y = __shfl_xor_sync(0xffffffffu, x, 1);
-                  // even lane: (x_a, x_b) = (x, y) -> x_a c - x_b s; odd lane: (x_a, x_b) = (y, x) -> x_b c + x_a s
-                  if (j < jn)
-                    st_global_b16(ob + static_cast<size_t>(j) * args.ldo, odd ? x * c + y * sn : x * c - y * sn);
-                  const float c1 = c * ct - sn * st;
-                  sn = sn * ct + c * st;
-                  c = c1;
+                  const float2 r2 = *reinterpret_cast<const float2*>(rsb + c0 + j);  // broadcast
+                  float xA, xB;
+                  mul2(__uint_as_float(acc[j]), __uint_as_float(acc[j + 1]), r2.x * cs, r2.y * cs, xA, xB);
+                  const float yA = __shfl_xor_sync(0xffffffffu, xA, 1);
+                  const float yB = __shfl_xor_sync(0xffffffffu, xB, 1);
+                  float oA, oB;
+                  mul2(xA, xB, cA, cB, oA, oB);
+                  fma2(yA, yB, sA, sB, oA, oB);
+                  // even lane: token j, channels (n, n + 1); odd lane: token j + 1, channels (n - 1, n)
+                  const float other = __shfl_xor_sync(0xffffffffu, odd ? oA : oB, 1);
+                  if (odd) {
+                    if (j + 1 < jn) st_global_b32(ob - 1 + static_cast<size_t>(j + 1) * args.ldo, pack_bf16x2(other, oB));
+                  } else {
+                    if (j < jn) st_global_b32(ob + static_cast<size_t>(j) * args.ldo, pack_bf16x2(oA, other));
+                  }
+                  // both tokens two positions on
+                  float nA, nB, mA, mB;
+                  mul2(cA, cB, ct2, ct2, nA, nB);
+                  fma2(sA, sB, -st2, -st2, nA, nB);
+                  mul2(sA, sB, ct2, ct2, mA, mB);
+                  fma2(cA, cB, st2, st2, mA, mB);
+                  cA = nA;
+                  cB = nB;
+                  sA = mA;
+                  sB = mB;
                 }
               }
             } else {
@@ -470,10 +535,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               }
             }
           } else {
+            // adjacent lanes swap one value per token pair and each stores two channels of one token
+            const bool odd = (lane & 1) != 0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < jn)
-                st_global_b16(ob + static_cast<size_t>(j) * args.ldo, __uint_as_float(acc[j]) * rsb[c0 + j] * cs);
+            for (int j = 0; j < 32; j += 2) {
+              const float2 r2 = *reinterpret_cast<const float2*>(rsb + c0 + j);  // broadcast
+              float xA, xB;
+              mul2(__uint_as_float(acc[j]), __uint_as_float(acc[j + 1]), r2.x * cs, r2.y * cs, xA, xB);
+              const float other = __shfl_xor_sync(0xffffffffu, odd ? xA : xB, 1);
+              if (odd) {
+                if (j + 1 < jn) st_global_b32(ob - 1 + static_cast<size_t>(j + 1) * args.ldo, pack_bf16x2(other, xB));
+              } else {
+                if (j < jn) st_global_b32(ob + static_cast<size_t>(j) * args.ldo, pack_bf16x2(xA, other));
+              }
+            }
           }
         } else {  // COLSCALE
           __nv_bfloat16* ob = args.out + static_cast<size_t>(tokc) * args.ldo + n;

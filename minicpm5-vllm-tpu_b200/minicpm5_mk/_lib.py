@@ -9,7 +9,8 @@ import ctypes
 import os
 
 LIB_NAME = "libminicpm5_mk.so"
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+# MINICPM5_MK_LIB overrides the library path (a build kept elsewhere, e.g. for A/B timing of two builds)
+LIB_PATH = os.environ.get("MINICPM5_MK_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 # Every symbol declared in include/minicpm5_mk.h.
 EXPORTED = (
