@@ -43,6 +43,7 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
 struct DeviceState {
   bool ready = false;
   int sm_count = 0;
+  int pair_clusters[2] = {0, 0};  // co-resident 2-CTA clusters of the pair GEMM (int8, bf16 weights)
   int* err = nullptr;
 };
 
@@ -85,6 +86,37 @@ mk_status device_state(DeviceState** out) {
                     mk::gemm_w8a16_kernel<MK_GEMM_RESID32, true>})
       MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(mk::gemm_smem_bytes(true))));
+    for (auto fn : {mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE, false, true>, mk::gemm_w8a16_kernel<MK_GEMM_RESID, false, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU, false, true>, mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE, false, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_RESID32, false, true>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(mk::gemm_smem_bytes(false))));
+    for (auto fn : {mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE, true, true>, mk::gemm_w8a16_kernel<MK_GEMM_RESID, true, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_SWIGLU, true, true>, mk::gemm_w8a16_kernel<MK_GEMM_COLSCALE, true, true>,
+                    mk::gemm_w8a16_kernel<MK_GEMM_RESID32, true, true>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(mk::gemm_smem_bytes(true))));
+    // how many CTA pairs fit on the GPU at once (clusters must sit in one GPC, so an odd SM of a GPC
+    // stays out): the persistent pair GEMM launches that many
+    for (int wb = 0; wb < 2; ++wb) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (d.sm_count / 2));
+      cfg.blockDim = dim3(mk::G_THREADS);
+      cfg.dynamicSmemBytes = mk::gemm_smem_bytes(wb == 1);
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      const cudaError_t e =
+          wb ? cudaOccupancyMaxActiveClusters(&n, mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE, true, true>, &cfg)
+             : cudaOccupancyMaxActiveClusters(&n, mk::gemm_w8a16_kernel<MK_GEMM_ROWSCALE, false, true>, &cfg);
+      d.pair_clusters[wb] = e == cudaSuccess && n > 0 ? n : 0;
+      if (e != cudaSuccess) (void)cudaGetLastError();
+    }
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(mk::TA_SMEM)));
     MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -124,6 +156,26 @@ mk_status launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...) == cudaSuccess ? MK_OK : MK_ERR_CUDA;
 }
+// The same with clusters of two CTAs along x (grid.x even).
+template <typename... KArgs, typename... Args>
+mk_status launch_k_pair(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                        Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...) == cudaSuccess ? MK_OK : MK_ERR_CUDA;
+}
 
 // Tokens per GEMM tile for M tokens and N output channels on `sms` SMs.  The persistent GEMM runs
 // ceil(tiles / sms) waves of tiles; a tile of nt tokens costs about nt + 32 token-steps (the weight tile's
@@ -149,7 +201,20 @@ int choose_nt(int M, int N, int sms) {
   return best;
 }
 
-// Token operand: bf16 [rows, ld], box 64 (K) x nt (tokens per tile), 128-byte swizzle.
+// A GEMM of M tokens and N output channels runs on CTA pairs (2-SM UMMAs over 256 channels) when N is a
+// multiple of 256 and M is more than a few rows.  The choice depends on N only once M > 64, so every
+// forward shape of one projection (any batch, sequence-parallel rank rows) takes the same path.
+bool pair_gemm(int M, int N) { return N % (2 * mk::GW) == 0 && M > 64; }
+// Tokens per tile: choose_nt, but a multiple of 32 for pairs (2-SM UMMA N) also below GT tokens.
+int plan_nt(int M, int N, int sms) {
+  if (pair_gemm(M, N) && M < mk::GT) return ((M + 31) / 32) * 32;
+  return choose_nt(M, N, sms);
+}
+// Rows of the token tensor map's box: a pair CTA loads half of the tile.
+int a_box(int M, int N, int nt) { return pair_gemm(M, N) ? nt / 2 : nt; }
+
+// Token operand: bf16 [rows, ld], box 64 (K) x nt rows (tokens per tile, or half of them for a CTA pair),
+// 128-byte swizzle.
 mk_status map_a(CUtensorMap* m, const void* a, int rows, int K, int ld, int nt = 0) {
   if (nt <= 0) nt = mk::gemm_nt(rows);
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
@@ -200,7 +265,7 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.M = M;
   ga.N = N;
   ga.K = K;
-  ga.nt = fu.nt > 0 ? fu.nt : mk::gemm_nt(M);
+  ga.nt = fu.nt > 0 ? fu.nt : plan_nt(M, N, d->sm_count);
   ga.mode = mode;
   ga.row_scale = row_scale;
   ga.col_scale = col_scale;
@@ -222,14 +287,21 @@ mk_status launch_gemm(const DeviceState* d, const CUtensorMap& ma, const CUtenso
   ga.rope_pos_base = fu.rope_pos_base;
   ga.sp = fu.sp;
   ga.err = d->err;
+  const bool pair = pair_gemm(M, N) && d->pair_clusters[fu.wbf16 ? 1 : 0] > 0;
+  if (pair_gemm(M, N) && !pair) return MK_ERR_CUDA;  // the token map was built for pairs
+  if (pair && ga.nt % 32) return MK_ERR_BAD_SHAPE;
   const int tiles = ((M + ga.nt - 1) / ga.nt) * (N / mk::GW);
-  const int grid = std::max(1, std::min(tiles, d->sm_count));
+  const int grid = pair ? 2 * std::max(1, std::min(tiles / 2, d->pair_clusters[fu.wbf16 ? 1 : 0]))
+                        : std::max(1, std::min(tiles, d->sm_count));
   const dim3 g(grid), b(mk::G_THREADS);
   const bool pdl = fu.pdl;
   const size_t smem = mk::gemm_smem_bytes(fu.wbf16);
-#define MK_GEMM_CASE(MODE)                                                                          \
-  case MODE:                                                                                        \
-    return fu.wbf16 ? launch_k(mk::gemm_w8a16_kernel<MODE, true>, g, b, smem, st, pdl, ma, mb, ga)  \
+#define MK_GEMM_CASE(MODE)                                                                                      \
+  case MODE:                                                                                                    \
+    if (pair)                                                                                                   \
+      return fu.wbf16 ? launch_k_pair(mk::gemm_w8a16_kernel<MODE, true, true>, g, b, smem, st, pdl, ma, mb, ga) \
+                      : launch_k_pair(mk::gemm_w8a16_kernel<MODE, false, true>, g, b, smem, st, pdl, ma, mb, ga); \
+    return fu.wbf16 ? launch_k(mk::gemm_w8a16_kernel<MODE, true>, g, b, smem, st, pdl, ma, mb, ga)              \
                     : launch_k(mk::gemm_w8a16_kernel<MODE, false>, g, b, smem, st, pdl, ma, mb, ga);
   switch (mode) {
     MK_GEMM_CASE(MK_GEMM_ROWSCALE)
@@ -562,17 +634,19 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
 
   // token tiles sized per projection (choose_nt); one token tensor map per (buffer, tile size)
   const int sms = d->sm_count;
-  const int nt_qkv = choose_nt(T, nqkv, sms), nt_o = choose_nt(T, H, sms), nt_gu = choose_nt(T, 2 * I, sms);
-  const int nt_down = nt_o, nt_kv = choose_nt(T, 2 * kvd, sms);
-  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mal, mhl;
-  MK_TRY(map_a(&mx_qkv, xb, T, H, H, nt_qkv));
-  MK_TRY(map_a(&mx_gu, xb, T, H, H, nt_gu));
-  MK_TRY(map_a(&mx_kv, xb, T, H, H, nt_kv));
-  MK_TRY(map_a(&mattn, attn, T, qd, qd, nt_o));
-  MK_TRY(map_a(&mh, hb, T, I, I, nt_down));
-  MK_TRY(map_a(&mxl, xlb, bs, H, H));
-  MK_TRY(map_a(&mal, al, bs, qd, qd));
-  MK_TRY(map_a(&mhl, hl, bs, I, I));
+  const int nt_qkv = plan_nt(T, nqkv, sms), nt_o = plan_nt(T, H, sms), nt_gu = plan_nt(T, 2 * I, sms);
+  const int nt_down = nt_o, nt_kv = plan_nt(T, 2 * kvd, sms);
+  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mxl_gu, mal, mhl;
+  MK_TRY(map_a(&mx_qkv, xb, T, H, H, a_box(T, nqkv, nt_qkv)));
+  MK_TRY(map_a(&mx_gu, xb, T, H, H, a_box(T, 2 * I, nt_gu)));
+  MK_TRY(map_a(&mx_kv, xb, T, H, H, a_box(T, 2 * kvd, nt_kv)));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd, a_box(T, H, nt_o)));
+  MK_TRY(map_a(&mh, hb, T, I, I, a_box(T, H, nt_down)));
+  // the last rows' projections (bs rows); each map's box follows its GEMM's plan
+  MK_TRY(map_a(&mxl, xlb, bs, H, H, a_box(bs, qd, plan_nt(bs, qd, sms))));
+  MK_TRY(map_a(&mxl_gu, xlb, bs, H, H, a_box(bs, 2 * I, plan_nt(bs, 2 * I, sms))));
+  MK_TRY(map_a(&mal, al, bs, qd, qd, a_box(bs, H, plan_nt(bs, H, sms))));
+  MK_TRY(map_a(&mhl, hl, bs, I, I, a_box(bs, H, plan_nt(bs, H, sms))));
   auto tiles = [](GemmFusion f, int nt) {
     f.nt = nt;
     return f;
@@ -667,7 +741,7 @@ mk_status forward_impl(mk_handle* h, const int32_t* d_ids, int32_t bs, int32_t s
     MK_TRY(launch_k(mk::attn_last_combine_kernel, dim3(c.n_q, bs), dim3(mk::AL_HDMAX), 0, st, true, al, la));
     MK_TRY(launch_gemm(d, mal, h->m_o[l], bs, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
-    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+    MK_TRY(launch_gemm(d, mxl_gu, h->m_gu[l], bs, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], bs, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
@@ -770,15 +844,16 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
   const size_t kv_row_bytes = static_cast<size_t>(2 * kvd) * 2;
 
   const int sms = d->sm_count;
-  const int nt_qkv = choose_nt(T, nqkv, sms), nt_o = choose_nt(T, H, sms), nt_gu = choose_nt(T, 2 * I, sms);
-  const int nt_down = nt_o, nt_kv = choose_nt(T, 2 * kvd, sms);
-  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mal, mhl;
-  MK_TRY(map_a(&mx_qkv, xb, T, H, H, nt_qkv));
-  MK_TRY(map_a(&mx_gu, xb, T, H, H, nt_gu));
-  MK_TRY(map_a(&mx_kv, xb, T, H, H, nt_kv));
-  MK_TRY(map_a(&mattn, attn, T, qd, qd, nt_o));
-  MK_TRY(map_a(&mh, hb, T, I, I, nt_down));
+  const int nt_qkv = plan_nt(T, nqkv, sms), nt_o = plan_nt(T, H, sms), nt_gu = plan_nt(T, 2 * I, sms);
+  const int nt_down = nt_o, nt_kv = plan_nt(T, 2 * kvd, sms);
+  CUtensorMap mx_qkv, mx_gu, mx_kv, mattn, mh, mxl, mxl_gu, mal, mhl;
+  MK_TRY(map_a(&mx_qkv, xb, T, H, H, a_box(T, nqkv, nt_qkv)));
+  MK_TRY(map_a(&mx_gu, xb, T, H, H, a_box(T, 2 * I, nt_gu)));
+  MK_TRY(map_a(&mx_kv, xb, T, H, H, a_box(T, 2 * kvd, nt_kv)));
+  MK_TRY(map_a(&mattn, attn, T, qd, qd, a_box(T, H, nt_o)));
+  MK_TRY(map_a(&mh, hb, T, I, I, a_box(T, H, nt_down)));
   MK_TRY(map_a(&mxl, xlb, 1, H, H));
+  MK_TRY(map_a(&mxl_gu, xlb, 1, H, H));
   MK_TRY(map_a(&mal, al, 1, qd, qd));
   MK_TRY(map_a(&mhl, hl, 1, I, I));
   auto tiles = [](GemmFusion f, int nt) {
@@ -895,7 +970,7 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
     MK_TRY(launch_k(mk::attn_last_combine_kernel, dim3(c.n_q, 1), dim3(mk::AL_HDMAX), 0, st, true, al, la));
     MK_TRY(launch_gemm(d, mal, h->m_o[l], 1, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
-    MK_TRY(launch_gemm(d, mxl, h->m_gu[l], 1, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
+    MK_TRY(launch_gemm(d, mxl_gu, h->m_gu[l], 1, 2 * I, H, MK_GEMM_SWIGLU, nullptr,
                        h->w.s_gu + static_cast<size_t>(l) * 2 * I, hl, I, 0.f, st, nullptr, 0, norm_from(rowsql)));
     MK_TRY(launch_gemm(d, mhl, h->m_down[l], 1, H, I, mk::GEMM_RESID32, nullptr,
                        h->w.s_down + static_cast<size_t>(l) * H, xlb, H, r, st, xl32, H, resid_stats_last));
@@ -1002,9 +1077,9 @@ mk_status mk_gemm_w8a16_fused(const void* a, int32_t M, int32_t K, int32_t lda, 
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || lda % 8 || ldo % 8 || lda < K) return MK_ERR_BAD_ALIGN;
   DeviceState* d = nullptr;
   MK_TRY(device_state(&d));
-  fu.nt = choose_nt(M, N, d->sm_count);
+  fu.nt = plan_nt(M, N, d->sm_count);
   CUtensorMap ma, mb;
-  MK_TRY(map_a(&ma, a, M, K, lda, fu.nt));
+  MK_TRY(map_a(&ma, a, M, K, lda, a_box(M, N, fu.nt)));
   MK_TRY(map_b(&mb, w, N, K, kWeightBoxRows, fu.wbf16));
   return launch_gemm(d, ma, mb, M, N, K, mode, row_scale, col_scale, out, ldo, resid_scale,
                      static_cast<cudaStream_t>(stream), resid32, ld_resid32, fu);

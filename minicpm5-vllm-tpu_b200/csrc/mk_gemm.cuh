@@ -151,23 +151,37 @@ __device__ __forceinline__ void st_global_b16(__nv_bfloat16* p, float v) {
 
 // WB: the weights are bf16 [N, K] instead of int8 (the same kernel without quantisation: the weight
 // tiles arrive as two 64-K panels and the converter warps copy them into TMEM unchanged).
-template <int MODE, bool WB = false>
+//
+// PAIR: a cluster of two CTAs computes 256 output channels x nt tokens with 2-SM UMMAs (M = 256):
+// each CTA converts its own 128 channels' weights into its TMEM and loads its half of the token tile
+// (nt/2 rows; the token tensor map's box is nt/2 high), so each SM streams half the token bytes per
+// FLOP.  The even CTA's MMA warp issues the MMAs; the token panels of both CTAs complete on the even
+// CTA's x_full, both CTAs' converters and epilogues arrive on the even CTA's w_full and tempty, and its
+// commits arrive on the barriers of both CTAs.  Each CTA's epilogue drains its own 128 channels.
+template <int MODE, bool WB = false, bool PAIR = false>
 __global__ void __launch_bounds__(G_THREADS, 1)
     gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                       const GemmArgs args) {
   constexpr int QS = gq_slots(WB);
   constexpr uint32_t QB = gq_bytes(WB);
+  // Token ring: 3 slots of a whole tile's 128-K stage, or for a pair CTA (which loads half the tile's
+  // rows) 6 slots in the same shared memory.  A token load takes about 2400 cycles to land whatever its
+  // size, so the deeper ring is what lets the pair's MMAs run without waiting for it.
+  constexpr int XS = PAIR ? 2 * GX_SLOTS : GX_SLOTS;
+  constexpr uint32_t XSUB = PAIR ? G_XSUB_BYTES / 2 : G_XSUB_BYTES;  // one 64-K panel of the slot
+  constexpr uint32_t XB = 2 * XSUB;
+  static_assert(XS * XB == GX_SLOTS * G_X_BYTES && XSUB % 1024 == 0, "token ring layout");
   extern __shared__ uint8_t g_smem_raw[];
   const uint32_t raw = smem_u32(g_smem_raw);
   uint8_t* sbase = g_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sX = sbase;                                     // [GX_SLOTS] token tiles
-  uint8_t* sQ = sX + GX_SLOTS * G_X_BYTES;                 // [QS] weight tiles
+  uint8_t* sX = sbase;                                     // [XS] token stages
+  uint8_t* sQ = sX + XS * XB;                              // [QS] weight tiles
   float* rs_s = reinterpret_cast<float*>(sQ + QS * QB);    // [2][GT]
   float* ss_s = rs_s + G_RS_FLOATS;                                    // [2][4][GT]
   uint64_t* bars = reinterpret_cast<uint64_t*>(ss_s + G_SS_FLOATS);
-  uint64_t* x_full = bars;                   // [GX_SLOTS] TMA landed
-  uint64_t* x_empty = x_full + GX_SLOTS;     // [GX_SLOTS] MMAs reading the slot finished
-  uint64_t* q_full = x_empty + GX_SLOTS;     // [QS] TMA landed
+  uint64_t* x_full = bars;                   // [XS] TMA landed
+  uint64_t* x_empty = x_full + XS;           // [XS] MMAs reading the slot finished
+  uint64_t* q_full = x_empty + XS;           // [QS] TMA landed
   uint64_t* q_empty = q_full + QS;           // [QS] converters read the slot
   uint64_t* w_full = q_empty + QS;           // [GW_SLOTS] converters wrote the TMEM weight slot
   uint64_t* w_empty = w_full + GW_SLOTS;     // [GW_SLOTS] MMAs reading the TMEM slot finished
@@ -180,9 +194,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;  // 0: the pair's MMA-issuing CTA
+  // shared::cluster address of this CTA's barrier `b` in the even CTA / in the odd CTA
+  auto lead_bar = [&](uint64_t* b) { return PAIR ? mapa_cluster(smem_u32(b), 0) : smem_u32(b); };
+  auto peer_bar = [&](uint64_t* b) { return mapa_cluster(smem_u32(b), 1); };
+  constexpr uint32_t kPairArrivals = PAIR ? 2 : 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GX_SLOTS; ++s) {
+    for (int s = 0; s < XS; ++s) {
       mbar_init(&x_full[s], 1);
       mbar_init(&x_empty[s], 1);
     }
@@ -191,12 +210,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       mbar_init(&q_empty[s], G_CONV_WARPS);
     }
     for (int s = 0; s < GW_SLOTS; ++s) {
-      mbar_init(&w_full[s], G_CONV_WARPS);
+      mbar_init(&w_full[s], G_CONV_WARPS * kPairArrivals);
       mbar_init(&w_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], G_EPI_WARPS);
+      mbar_init(&tempty[a], G_EPI_WARPS * kPairArrivals);
       mbar_init(&esync[a], G_EPI_WARPS);
     }
     mbar_init(drain, 1);
@@ -206,22 +225,36 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, G_TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, G_TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, G_TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers and TMEM exist before either signals the other
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_trigger();
 
   const int nt = args.nt;
-  const int num_c = args.N / GW;                 // channel tiles
+  const int num_c = args.N / GW;                 // 128-channel tiles
+  const int num_u = PAIR ? num_c / 2 : num_c;    // channel units of a token tile (256 channels per pair)
   const int num_t = (args.M + nt - 1) / nt;      // token tiles
-  const int num_tiles = num_t * num_c;
+  const int num_tiles = num_t * num_u;
   const int KT = (args.K + GK - 1) / GK;  // K % 64 == 0; a last half stage covers K % 128 == 64
-  const int my_tiles = (num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                       static_cast<int>(gridDim.x);
+  const int unit = PAIR ? static_cast<int>(blockIdx.x) >> 1 : static_cast<int>(blockIdx.x);  // CTA or pair
+  const int nunits = PAIR ? static_cast<int>(gridDim.x) >> 1 : static_cast<int>(gridDim.x);
+  const int my_tiles = (num_tiles - unit + nunits - 1) / nunits;
+  // token tile and 128-channel tile of this CTA in its it-th tile
+  auto tile_tb = [&](int it) { return (unit + it * nunits) / num_u; };
+  auto tile_cb = [&](int it) {
+    const int u = (unit + it * nunits) % num_u;
+    return PAIR ? 2 * u + static_cast<int>(crank) : u;
+  };
   const int total = my_tiles * KT;  // k-steps this CTA runs (slot index = k-step mod ring size)
 
   if (warp == 0 || warp == G_QPROD_WARP) {
@@ -235,79 +268,113 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // the token tiles come from the previous kernel; the weights are constant, so their producer (and the
     // converters and the MMA warp, which touch no global memory) start before the previous kernel ends
     if (is_x) pdl_wait();
-    const int slots = is_x ? GX_SLOTS : QS;
+    const int slots = is_x ? XS : QS;
     uint64_t* full = is_x ? x_full : q_full;
     uint64_t* empty = is_x ? x_empty : q_empty;
+    // X panel bytes of the whole tile (a pair's two halves together complete the even CTA's x_full)
     const uint32_t x_panel = static_cast<uint32_t>(nt) * GKB * 2;
+    const int x_row0 = PAIR ? static_cast<int>(crank) * (nt / 2) : 0;  // this CTA's half of the tile
     uint32_t issued = 0, issued_par = 0;
     for (int idx = 0; idx < total; ++idx) {
       const int s = idx % slots;
       const uint32_t ph = (idx / slots) & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, abort_flag))) break;
-      const int tile = blockIdx.x + (idx / KT) * gridDim.x;
+      const int it = idx / KT;
       const int kt = idx % KT;
       if (leader) {
         if (is_x) {
           const bool two = args.K - kt * GK > GKB;
-          mbar_arrive_expect_tx(&full[s], two ? 2 * x_panel : x_panel);
-          tma_load_2d(sX + s * G_X_BYTES, &tmX, &full[s], kt * GK, (tile / num_c) * nt);
-          if (two) tma_load_2d(sX + s * G_X_BYTES + G_XSUB_BYTES, &tmX, &full[s], kt * GK + GKB, (tile / num_c) * nt);
+          const int row = tile_tb(it) * nt + x_row0;
+          if constexpr (PAIR) {
+            if (crank == 0) mbar_arrive_expect_tx(&full[s], two ? 2 * x_panel : x_panel);
+            const uint32_t fb = lead_bar(&full[s]);
+            tma_load_2d_pair(sX + s * XB, &tmX, fb, kt * GK, row);
+            if (two) tma_load_2d_pair(sX + s * XB + XSUB, &tmX, fb, kt * GK + GKB, row);
+          } else {
+            mbar_arrive_expect_tx(&full[s], two ? 2 * x_panel : x_panel);
+            tma_load_2d(sX + s * XB, &tmX, &full[s], kt * GK, row);
+            if (two) tma_load_2d(sX + s * XB + XSUB, &tmX, &full[s], kt * GK + GKB, row);
+          }
         } else {
           // int8: one 128 x 128 box; bf16: two 128-row x 64-K boxes.  A half last stage reads zeros
           // past K.
           mbar_arrive_expect_tx(&full[s], QB);
-          tma_load_2d(sQ + s * QB, &tmW, &full[s], kt * GK, (tile % num_c) * GW);
-          if (WB) tma_load_2d(sQ + s * QB + G_Q_BYTES, &tmW, &full[s], kt * GK + GKB, (tile % num_c) * GW);
+          tma_load_2d(sQ + s * QB, &tmW, &full[s], kt * GK, tile_cb(it) * GW);
+          if (WB) tma_load_2d(sQ + s * QB + G_Q_BYTES, &tmW, &full[s], kt * GK + GKB, tile_cb(it) * GW);
         }
       }
       __syncwarp();
       issued |= 1u << s;
       issued_par = (issued_par & ~(1u << s)) | (ph << s);
     }
-    // Every issued copy must land before the CTA may exit.
-    for (int i = 0; i < slots; ++i)
-      if (issued & (1u << i)) mbar_wait_drain(&full[i], (issued_par >> i) & 1u);
+    // Every issued copy must land before the CTA may exit.  (An odd CTA's token panels complete on the
+    // even CTA's barrier, which waits for both halves; the pair leaves together after a cluster barrier.)
+    if (!PAIR || crank == 0 || !is_x)
+      for (int i = 0; i < slots; ++i)
+        if (issued & (1u << i)) mbar_wait_drain(&full[i], (issued_par >> i) & 1u);
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop, so TMEM addresses and smem descriptors are warp-uniform values
     // (uniform registers feed tcgen05.mma directly); one elected lane issues the tcgen05 ops.
     const bool leader = elect_one();
-    const uint32_t idesc = idesc_bf16_f32(GW, nt);
+    const uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * GW : GW, nt);
     int idx = 0;
-    bool ok = true;
+    bool ok = !PAIR || crank == 0;  // the odd CTA of a pair issues nothing
+    // arrive (on both CTAs' copies for a pair) when the MMAs issued so far have completed
+    auto commit_all = [&](uint64_t* b) {
+      if constexpr (PAIR) {
+        mma_commit_pair(smem_u32(b));
+        mma_commit_pair(peer_bar(b));
+      } else {
+        mma_commit(b);
+      }
+    };
+    auto wait_cl = [&](uint64_t* b, uint32_t par) { return mbar_wait(b, par, abort_flag); };
     for (int it = 0; ok && it < my_tiles; ++it) {
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tempty[a], aph ^ 1u, abort_flag))) break;
+      if (!__all_sync(0xffffffffu, wait_cl(&tempty[a], aph ^ 1u))) break;
       tc_fence_after();
       const uint32_t d = tmem_base + a * GT;
       for (int kt = 0; kt < KT; ++kt, ++idx) {
-        const int sx = idx % GX_SLOTS, sw = idx % GW_SLOTS;
-        ok = __all_sync(0xffffffffu, mbar_wait(&x_full[sx], (idx / GX_SLOTS) & 1, abort_flag) &&
-                                         mbar_wait(&w_full[sw], (idx / GW_SLOTS) & 1, abort_flag));
+        const int sx = idx % XS, sw = idx % GW_SLOTS;
+        ok = __all_sync(0xffffffffu, wait_cl(&x_full[sx], (idx / XS) & 1) &&
+                                         wait_cl(&w_full[sw], (idx / GW_SLOTS) & 1));
         if (!ok) break;
         tc_fence_after();
-        const uint64_t db0 = sdesc_kmajor_sw128(smem_u32(sX + sx * G_X_BYTES));
-        const uint64_t db1 = sdesc_kmajor_sw128(smem_u32(sX + sx * G_X_BYTES + G_XSUB_BYTES));
+        const uint64_t db0 = sdesc_kmajor_sw128(smem_u32(sX + sx * XB));
+        const uint64_t db1 = sdesc_kmajor_sw128(smem_u32(sX + sx * XB + XSUB));
         const uint32_t wa = tmem_base + G_W_COL0 + sw * G_W_COLS;
         const int nk = args.K - kt * GK > GKB ? GK / 16 : GKB / 16;
         if (leader) {
 #pragma unroll
           for (int k = 0; k < GK / 16; ++k)
-            if (k < nk)
-              mma_f16_ts(d, wa + k * 8, (k < 4 ? db0 : db1) + 2 * (k & 3), idesc, (kt | k) != 0 ? 1u : 0u);
-          mma_commit(&x_empty[sx]);
-          mma_commit(&w_empty[sw]);
+            if (k < nk) {
+              const uint64_t db = (k < 4 ? db0 : db1) + 2 * (k & 3);
+              if constexpr (PAIR)
+                mma_f16_ts_pair(d, wa + k * 8, db, idesc, (kt | k) != 0 ? 1u : 0u);
+              else
+                mma_f16_ts(d, wa + k * 8, db, idesc, (kt | k) != 0 ? 1u : 0u);
+            }
+          commit_all(&x_empty[sx]);
+          commit_all(&w_empty[sw]);
         }
         __syncwarp();
       }
       if (!ok) break;
-      if (leader) mma_commit(&tfull[a]);
+      if (leader) commit_all(&tfull[a]);
       __syncwarp();
     }
-    if (leader) mma_commit(drain);
-    __syncwarp();
-    mbar_wait_drain(drain, 0);
+    if (!PAIR || crank == 0) {
+      if (leader) {
+        if constexpr (PAIR)
+          mma_commit_pair(smem_u32(drain));
+        else
+          mma_commit(drain);
+      }
+      __syncwarp();
+      mbar_wait_drain(drain, 0);
+    }
   } else if (warp < G_CONV_WARP0) {
     // -------------------------------------------------------------------- epilogue
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
@@ -317,8 +384,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const float r = args.resid_scale;
     pdl_wait();  // statistics, residual and outputs are shared with earlier kernels
     for (int it = 0; it < my_tiles; ++it) {
-      const int tile = blockIdx.x + it * gridDim.x;
-      const int tb = tile / num_c, cb = tile % num_c;
+      const int tb = tile_tb(it), cb = tile_cb(it);
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       const int tok0 = tb * nt;
@@ -328,8 +394,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         // is drained (the first tile also prefetches its own rows).
         for (int pt = (it == 0 ? 0 : 1); pt <= 1; ++pt) {
           if (it + pt >= my_tiles) break;
-          const int ptile = blockIdx.x + (it + pt) * gridDim.x;
-          const int ptok0 = (ptile / num_c) * nt, pcb = ptile % num_c;
+          const int ptok0 = tile_tb(it + pt) * nt, pcb = tile_cb(it + pt);
           for (int l = et; l < nt * 4; l += G_EPI_WARPS * 32) {
             const int tok = ptok0 + (l >> 2);
             if (tok < args.M)
@@ -560,7 +625,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       // accumulator drained: the MMAs of tile it + 2 may overwrite it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[a]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(lead_bar(&tempty[a]));
+        else
+          mbar_arrive(&tempty[a]);
+      }
       if (MODE == GEMM_RESID32 && args.rowsq) {
         // combine the four lane quarters' partial sums per token (fixed order) into the tile's statistic
         __syncwarp();
@@ -630,14 +700,26 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&w_full[sw]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(lead_bar(&w_full[sw]));
+        else
+          mbar_arrive(&w_full[sw]);
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, G_TMEM_COLS);
+  if constexpr (PAIR) {
+    // neither CTA frees its TMEM or leaves while the pair's MMAs may still read its operands
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, G_TMEM_COLS);
+  } else {
+    if (warp == 1) tmem_dealloc(tmem_base, G_TMEM_COLS);
+  }
   if (threadIdx.x == 0 && *abort_flag && args.err) atomicCAS(args.err, 0, DEV_ERR_TIMEOUT_GEMM);
 }
 
