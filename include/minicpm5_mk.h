@@ -160,6 +160,18 @@ typedef int32_t (*mk_allgather_fn)(void* ctx, const void* d_send, void* d_recv, 
  * 512, 256, 128, 64 with seq % (2 * world * blk) == 0 that holds whole attention query blocks. */
 int32_t mk_sp_block(const mk_handle* h, int32_t seq, int32_t world);
 
+/* Whether mk_forward_sp cuts the long causal key ranges of a rank's attention over several CTAs
+ * (enabled by default).  A rank owns few query blocks and their key ranges are very unequal (at 8 ranks
+ * one CTA would walk all of an 8192-token sequence's keys while the average SM has a fifth of that), so
+ * when a replay of the grid's dispatch says it pays, ranges are cut into near-equal parts whose partial
+ * results (unnormalised output, running max, row sum) a second kernel merges in a fixed order.  The merge
+ * rounds differently from a single pass, so with a split the logits agree with mk_forward to float
+ * rounding (the same greedy id in the tests) rather than bit for bit; disabled, mk_forward_sp is
+ * bit-identical to mk_forward.  Set it before mk_workspace_size_sp: the split keeps its partial results
+ * in the workspace.  No counterpart in the reference (its sequence parallelism spans the two
+ * TensorCores of one chip). */
+mk_status mk_set_sp_key_split(mk_handle* h, int32_t enabled);
+
 /* Bytes of workspace mk_forward_sp needs on each rank. */
 mk_status mk_workspace_size_sp(const mk_handle* h, int32_t seq, int32_t world, size_t* bytes);
 

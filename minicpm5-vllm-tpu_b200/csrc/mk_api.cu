@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
+#include <queue>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -117,10 +119,9 @@ mk_status device_state(DeviceState** out) {
       d.pair_clusters[wb] = e == cudaSuccess && n > 0 ? n : 0;
       if (e != cudaSuccess) (void)cudaGetLastError();
     }
-    MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::TA_SMEM)));
-    MK_CUDA(cudaFuncSetAttribute(mk::attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(mk::TA_SMEM)));
+    for (auto fn : {mk::attn_tc_kernel<96, false>, mk::attn_tc_kernel<128, false>, mk::attn_tc_kernel<96, true>,
+                    mk::attn_tc_kernel<128, true>})
+      MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(mk::TA_SMEM)));
     for (auto fn : {mk::lm_head_kernel<1>, mk::lm_head_kernel<2>, mk::lm_head_kernel<4>, mk::lm_head_kernel<8>})
       MK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLmSmemMax));
     if (!g_encode) {
@@ -345,10 +346,12 @@ int ilog2(int v) {
 // tcgen05 causal GQA attention (mk_attn_tc.cuh).  Queries (rows per sequence `rows`) and keys /
 // values (S per sequence) may live in different buffers; under sequence parallelism the queries are
 // a rank's zig-zag rows and K/V the rank-by-rank all-gather (`sp`).
+// kchunk > 0 (one sequence) cuts query blocks with more key tiles into ranges of at most kchunk tiles,
+// one CTA each; their partial results go to `part` and attn_split_combine_kernel merges them.
 mk_status launch_attn_split(const DeviceState* d, const void* q_base, int rows, int ld_q, int q_col, const void* kv_base,
                             int S, int ld_kv, int k_col, int v_col, int bs, int n_q, int n_kv, int hd, float scale_log2,
                             void* out, int ld_out, cudaStream_t st, const mk::SpLayout& sp = mk::SpLayout(),
-                            bool pdl = false) {
+                            bool pdl = false, int kchunk = 0, float* part = nullptr) {
   const int G = n_q / n_kv;
   const int qpt = 128 / G;
   if (rows % (2 * qpt) || S % mk::TA_BK) return MK_ERR_BAD_SHAPE;
@@ -367,11 +370,77 @@ mk_status launch_attn_split(const DeviceState* d, const void* q_base, int rows, 
   a.nqb = rows / (2 * qpt);
   a.ld_out = ld_out;
   a.scale_log2 = scale_log2;
+  a.kchunk = kchunk;
+  a.n_q = n_q;
+  a.part = part;
   a.err = d->err;
-  dim3 grid(a.nqb, n_kv, bs);
+  if (kchunk > 0 && (bs != 1 || !part)) return MK_ERR_BAD_ARG;
   auto* o = static_cast<__nv_bfloat16*>(out);
-  if (hd == 96) return launch_k(mk::attn_tc_kernel<96>, grid, dim3(mk::TA_THREADS), mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
-  return launch_k(mk::attn_tc_kernel<128>, grid, dim3(mk::TA_THREADS), mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
+  const dim3 blk(mk::TA_THREADS);
+  if (kchunk == 0) {
+    const dim3 grid(a.nqb, n_kv, bs);
+    if (hd == 96) return launch_k(mk::attn_tc_kernel<96, false>, grid, blk, mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
+    return launch_k(mk::attn_tc_kernel<128, false>, grid, blk, mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a);
+  }
+  // with a key split the grid is (key range, query block, KV head), as many ranges as any block needs
+  const dim3 grid(mk::ta_nsplit(S / mk::TA_BK, kchunk), a.nqb, n_kv), cgrid(a.nqb, n_kv, hd / 8);
+  if (hd == 96) {
+    MK_TRY(launch_k(mk::attn_tc_kernel<96, true>, grid, blk, mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a));
+    return launch_k(mk::attn_split_combine_kernel<96>, cgrid, dim3(256), 0, st, pdl, o, a);
+  }
+  MK_TRY(launch_k(mk::attn_tc_kernel<128, true>, grid, blk, mk::TA_SMEM, st, pdl, mq, mkm, mv, o, a));
+  return launch_k(mk::attn_split_combine_kernel<128>, cgrid, dim3(256), 0, st, pdl, o, a);
+}
+
+// Key tiles per attention CTA under sequence parallelism (0 = no split).  A rank holds few query blocks
+// and their causal key ranges are very unequal: at 4 and 8 ranks the longest CTA walks all 128 key tiles
+// of an 8192-token sequence while the rank's whole attention is 56 or 28 tiles per SM.  The choice
+// replays the grid's dispatch order (key ranges of a block together, heaviest blocks first, KV heads
+// outermost) on `sms` SMs: each CTA takes its start-up and drain (about 4.5 us, measured) plus 0.9 us per
+// key tile, an empty one 0.3 us, and goes to the SM that frees first; a split also pays the merge kernel
+// (about 5 us).  The smallest simulated time wins, and a split must gain 3 % to be used.  Planned on
+// rank 0's layout, so every rank sizes the same workspace.
+int sp_key_chunk(const mk_config& c, const mk::SpLayout& sp, int S, int sms) {
+  if (sp.world <= 1 || sms <= 0) return 0;
+  const int G = c.n_q / c.n_kv, qpt = 128 / G;
+  const int nqb = sp.rows_per_rank / (2 * qpt);
+  std::vector<int> ntot(nqb);
+  for (int y = 0; y < nqb; ++y) {  // dispatch order: heaviest (last local) block first
+    const int qb = nqb - 1 - y;
+    ntot[y] = (mk::sp_pos(sp, qb * 2 * qpt) + 2 * qpt - 1) / mk::TA_BK + 1;
+  }
+  auto makespan = [&](int kchunk) {
+    std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+    for (int i = 0; i < sms; ++i) free_at.push(0.0);
+    auto run = [&](double cost) {
+      const double t = free_at.top();
+      free_at.pop();
+      free_at.push(t + cost);
+    };
+    const int zmax = kchunk > 0 ? mk::ta_nsplit(S / mk::TA_BK, kchunk) : 1;
+    for (int g = 0; g < c.n_kv; ++g)
+      for (int y = 0; y < nqb; ++y) {
+        const int ns = mk::ta_nsplit(ntot[y], kchunk), per = mk::ta_split_per(ntot[y], ns);
+        for (int z = 0; z < zmax; ++z) run(z >= ns ? 0.3 : 4.5 + 0.9 * (std::min(ntot[y], z * per + per) - z * per));
+      }
+    double m = 0.0;
+    while (!free_at.empty()) {
+      m = std::max(m, free_at.top());
+      free_at.pop();
+    }
+    return m + (kchunk > 0 ? 5.0 : 0.0);
+  };
+  double best = makespan(0) * 0.97;
+  int best_k = 0;
+  for (int k : {8, 12, 16, 20, 24, 28, 32, 36, 40, 44, 48, 56, 64, 72, 80, 96, 112}) {
+    if (k >= S / mk::TA_BK) break;
+    const double m = makespan(k);
+    if (m < best) {
+      best = m;
+      best_k = k;
+    }
+  }
+  return best_k;
 }
 
 mk_status launch_attn(const DeviceState* d, const void* qkv, int bs, int S, int n_q, int n_kv, int hd, int ld_qkv,
@@ -407,6 +476,8 @@ struct mk_handle {
   mk_weight_ptrs w;
   int n_qkv = 0, q_dim = 0, kv_dim = 0;
   bool wbf16 = false;  // bf16 projection weights (weight_bits 16) instead of int8
+  bool sp_key_split = true;  // mk_forward_sp cuts long causal key ranges over several attention CTAs
+  mutable std::vector<std::array<int, 3>> sp_chunk_cache;  // (seq, world, key tiles per CTA) already planned
   std::vector<CUtensorMap> m_qkv, m_o, m_gu, m_down;  // per layer
   CUtensorMap m_kv_last, m_q_last;
 };
@@ -787,7 +858,8 @@ int sp_block(const mk_config& c, int seq, int world) {
 
 struct SpWorkspace {
   Workspace local;  // the single-sequence workspace of a rank's seq / world rows
-  size_t kv_send, kv_all, alpart, total;  // alpart: last-position attention partials over all seq keys
+  size_t kv_send, kv_all, alpart, apart, total;  // alpart: last-position attention partials over all seq keys
+  int kchunk = 0;   // key tiles per attention CTA (0: no key split); apart: the split ranges' partials
 };
 
 SpWorkspace plan_workspace_sp(const mk_handle* h, int seq, int world) {
@@ -798,8 +870,24 @@ SpWorkspace plan_workspace_sp(const mk_handle* h, int seq, int world) {
   w.kv_send = w.local.total;
   w.kv_all = align256(w.kv_send + T * kv_row);
   w.alpart = align256(w.kv_all + static_cast<size_t>(seq) * kv_row);
-  w.total = align256(w.alpart + static_cast<size_t>(h->cfg.n_q) * ((seq + mk::AL_KEYS - 1) / mk::AL_KEYS) *
+  w.apart = align256(w.alpart + static_cast<size_t>(h->cfg.n_q) * ((seq + mk::AL_KEYS - 1) / mk::AL_KEYS) *
                                     (h->cfg.head_dim + 2) * 4);
+  const int blk = sp_block(h->cfg, seq, world);
+  if (h->sp_key_split && blk > 0) {
+    w.kchunk = -1;
+    for (const auto& e : h->sp_chunk_cache)
+      if (e[0] == seq && e[1] == world) w.kchunk = e[2];
+    if (w.kchunk < 0) {
+      mk::SpLayout sp;  // rank 0's layout
+      sp.blk = blk;
+      sp.world = world;
+      sp.rows_per_rank = T;
+      w.kchunk = sp_key_chunk(h->cfg, sp, seq, h->dev->sm_count);
+      h->sp_chunk_cache.push_back({seq, world, w.kchunk});
+    }
+  }
+  const size_t nsplit = w.kchunk > 0 ? mk::ta_nsplit(seq / mk::TA_BK, w.kchunk) : 0;
+  w.total = align256(w.apart + nsplit * T * h->cfg.n_q * (h->cfg.head_dim + 4) * 4);
   return w;
 }
 
@@ -916,8 +1004,8 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
     MK_TRY(gather_kv(qkv + qd, nqkv));
     MK_TRY(mark(MK_STAGE_KV_GATHER, 0));
     MK_TRY(launch_attn_split(d, qkv, T, nqkv, 0, kv_all, seq, 2 * kvd, 0, kvd, 1, c.n_q, c.n_kv, hd, kLog2e, attn, qd,
-                             st, sp, true));
-    MK_TRY(mark(MK_STAGE_ATTN, 1));
+                             st, sp, true, sw.kchunk, f32(sw.apart)));
+    MK_TRY(mark(MK_STAGE_ATTN, sw.kchunk > 0 ? 2 : 1));
     MK_TRY(launch_gemm(d, mattn, h->m_o[l], T, H, qd, mk::GEMM_RESID32, nullptr,
                        h->w.s_o + static_cast<size_t>(l) * H, xb, H, r, st, x32, H, tiles(resid_stats, nt_o)));
     MK_TRY(mark(MK_STAGE_O, 1));
@@ -987,6 +1075,12 @@ mk_status forward_sp_impl(mk_handle* h, const int32_t* d_ids, int32_t seq, int32
 extern "C" {
 
 int32_t mk_sp_block(const mk_handle* h, int32_t seq, int32_t world) { return h ? sp_block(h->cfg, seq, world) : 0; }
+
+mk_status mk_set_sp_key_split(mk_handle* h, int32_t enabled) {
+  if (!h) return MK_ERR_BAD_ARG;
+  h->sp_key_split = enabled != 0;
+  return MK_OK;
+}
 
 mk_status mk_workspace_size_sp(const mk_handle* h, int32_t seq, int32_t world, size_t* bytes) {
   if (!h || !bytes) return MK_ERR_BAD_ARG;

@@ -79,10 +79,25 @@ struct AttnTcArgs {
   // Sequence parallelism (sp.blk > 0, bs = 1): the query rows are this rank's zig-zag rows (row m at
   // position sp_pos(sp, m)) and K/V is the rank-by-rank all-gather (position p at row sp_row(sp, p)).
   SpLayout sp;
+  // Key split (the KSPLIT instantiation, kchunk > 0, one sequence): a query block with more than kchunk
+  // key tiles is cut into ta_nsplit near-equal key ranges, one CTA each (blockIdx.x = range); such CTAs
+  // write the unnormalised O, the running max and the row sum to `part` ([range][row][n_q][hd + 4] f32)
+  // and attn_split_combine_kernel merges the ranges.  Query blocks of one range write `out` directly.
+  int kchunk;
+  int n_q;
+  float* part;
   int* err;
 };
 
-template <int HD>
+// Key ranges of a query block with ntot key tiles: nsplit ranges of `per` tiles (the last one may be
+// shorter); none is empty.
+__host__ __device__ __forceinline__ int ta_nsplit(int ntot, int kchunk) {
+  return kchunk > 0 ? (ntot + kchunk - 1) / kchunk : 1;
+}
+__host__ __device__ __forceinline__ int ta_split_per(int ntot, int nsplit) { return (ntot + nsplit - 1) / nsplit; }
+
+// KSPLIT: the key-split variant (AttnTcArgs::kchunk); the other instantiation keeps the plain code path.
+template <int HD, bool KSPLIT>
 __global__ void __launch_bounds__(TA_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ out, const AttnTcArgs a) {
@@ -108,13 +123,21 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = 1 << a.lg2G;
   const int qpt = 128 >> a.lg2G;  // queries per Q tile
-  const int qb = a.nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
+  // Grid (query block, KV head, sequence), heaviest blocks first; with the key split (key range, query
+  // block, KV head), so that the ranges of one block are dispatched together, heaviest blocks first.
+  const int qb = a.nqb - 1 - static_cast<int>(KSPLIT ? blockIdx.y : blockIdx.x);
   const int qrow0 = qb * 2 * qpt;      // first query row of the CTA (local)
   const int q0 = sp_pos(a.sp, qrow0);  // its position; the 2 * qpt rows share one zig-zag block
-  const int g = blockIdx.y;
-  const int tok0 = blockIdx.z * a.rows;  // query / output rows of this sequence
-  const int kv0 = blockIdx.z * a.S;      // K/V rows of this sequence
-  const int ntiles = (q0 + 2 * qpt - 1) / TA_BK + 1;
+  const int g = KSPLIT ? blockIdx.z : blockIdx.y;
+  const int seqi = KSPLIT ? 0 : static_cast<int>(blockIdx.z);
+  const int tok0 = seqi * a.rows;  // query / output rows of this sequence
+  const int kv0 = seqi * a.S;      // K/V rows of this sequence
+  const int ntot = (q0 + 2 * qpt - 1) / TA_BK + 1;  // key tiles up to the block's last position
+  const int nsplit = KSPLIT ? ta_nsplit(ntot, a.kchunk) : 1;
+  const int chunk = KSPLIT ? static_cast<int>(blockIdx.x) : 0;
+  if (chunk >= nsplit) return;  // the whole CTA: this block has fewer key ranges
+  const int kt0 = chunk * ta_split_per(ntot, nsplit);  // first key tile of this CTA's range
+  const int ntiles = min(ntot, kt0 + ta_split_per(ntot, nsplit)) - kt0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -169,7 +192,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       if (leader) {
         mbar_arrive_expect_tx(&k_full[st], 2 * TA_KCHUNK);
         // a 64-key tile never straddles a zig-zag block (blocks are multiples of 64 tokens)
-        const int krow = kv0 + sp_row(a.sp, j * TA_BK);
+        const int krow = kv0 + sp_row(a.sp, (kt0 + j) * TA_BK);
         for (int c = 0; c < 2; ++c) tma_load_3d(sst + c * TA_KCHUNK, &tmK, &k_full[st], c * 64, g, krow);
         mbar_arrive_expect_tx(&v_full[st], 2 * TA_KCHUNK);
         for (int c = 0; c < 2; ++c)
@@ -310,7 +333,9 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       tmem_ld_32x32b_x32(tS + b * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld_32x32b_x32(tS + b * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_ld_wait();
-      const int valid = query - j * TA_BK + 1;  // keys of this tile visible to this row
+      // keys of this tile visible to this row (every range starts at or before the block's first
+      // position, so each row sees at least the first key of its range)
+      const int valid = query - (kt0 + j) * TA_BK + 1;
       if (valid < TA_BK) {
 #pragma unroll
         for (int e = 0; e < 64; ++e)
@@ -376,7 +401,25 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[t * 2 + b]);
     }
-    if (ok && mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag)) {
+    const bool fin = ok && mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag);
+    if (KSPLIT && fin && nsplit > 1) {
+      // one key range of a split block: unnormalised O, the max its exponentials are taken against
+      // (log2 units) and the row sum, for attn_split_combine_kernel
+      tc_fence_after();
+      float* pp = a.part + ((static_cast<size_t>(chunk) * a.rows + qrow0 + (query - q0)) * a.n_q + head) * (HD + 4);
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o32[32];
+        tmem_ld_32x32b_x32(tO + c * 32, o32);
+        tmem_ld_wait();
+        float4* d4 = reinterpret_cast<float4*>(pp + c * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          d4[q] = make_float4(__uint_as_float(o32[4 * q]), __uint_as_float(o32[4 * q + 1]),
+                              __uint_as_float(o32[4 * q + 2]), __uint_as_float(o32[4 * q + 3]));
+      }
+      *reinterpret_cast<float4*>(pp + HD) = make_float4(m_used, l, 0.f, 0.f);
+    } else if (fin) {
       tc_fence_after();
       const float inv = 1.f / l;
       __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + qrow0 + (query - q0)) * a.ld_out + head * HD;
@@ -401,6 +444,53 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
   if (threadIdx.x == 0 && *abort_flag && a.err) atomicCAS(a.err, 0, DEV_ERR_TIMEOUT_ATTN_TC);
+}
+
+// Merges the key ranges of split query blocks (AttnTcArgs::kchunk): for each (query, head) row,
+// M = max_s m_s, O = sum_s 2^(m_s - M) O_s, L = sum_s 2^(m_s - M) l_s, out = bf16(O / L), with the ranges
+// taken in order, so the result does not depend on which CTA finished first.  Grid (query block, KV head,
+// 8-dimension segment); thread = (query, head) row of the block, which reads one 32-byte sector of each
+// range's partial row.  Blocks of one range have nothing to merge.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_split_combine_kernel(__nv_bfloat16* __restrict__ out, const AttnTcArgs a) {
+  pdl_trigger();
+  // Every CTA waits for the attention grid, also those with nothing to merge: the next kernel waits only
+  // for this grid, and reads the rows the attention kernel wrote directly.
+  pdl_wait();
+  const int G = 1 << a.lg2G;
+  const int qpt = 128 >> a.lg2G;
+  const int qb = a.nqb - 1 - static_cast<int>(blockIdx.x);
+  const int qrow0 = qb * 2 * qpt;
+  const int q0 = sp_pos(a.sp, qrow0);
+  const int ntot = (q0 + 2 * qpt - 1) / TA_BK + 1;
+  const int nsplit = ta_nsplit(ntot, a.kchunk);
+  if (nsplit == 1) return;
+  const int c = static_cast<int>(blockIdx.z) * 8;  // first dimension of the segment
+  const size_t stride = static_cast<size_t>(a.rows) * a.n_q * (HD + 4);
+  for (int p = threadIdx.x; p < 2 * qpt * G; p += blockDim.x) {
+    const int row = qrow0 + (p >> a.lg2G);
+    const int head = static_cast<int>(blockIdx.y) * G + (p & (G - 1));
+    const float* p0 = a.part + (static_cast<size_t>(row) * a.n_q + head) * (HD + 4);
+    float mx = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p0[s * stride + HD]);
+    float L = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nsplit; ++s) {
+      const float* ps = p0 + s * stride;
+      const float w = exp2f(ps[HD] - mx);
+      L += w * ps[HD + 1];
+      const float4 v0 = *reinterpret_cast<const float4*>(ps + c);
+      const float4 v1 = *reinterpret_cast<const float4*>(ps + c + 4);
+      o[0] += w * v0.x; o[1] += w * v0.y; o[2] += w * v0.z; o[3] += w * v0.w;
+      o[4] += w * v1.x; o[5] += w * v1.y; o[6] += w * v1.z; o[7] += w * v1.w;
+    }
+    const float inv = 1.f / L;
+    uint4 pk;
+    pk.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+    pk.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+    pk.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+    pk.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * a.ld_out + head * HD + c) = pk;
+  }
 }
 
 }  // namespace mk

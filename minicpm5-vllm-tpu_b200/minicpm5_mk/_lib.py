@@ -18,7 +18,7 @@ EXPORTED = (
     "mk_get_error", "mk_destroy", "mk_gemm_w8a16", "mk_attention_prefill", "mk_rope", "mk_rms_rstd", "mk_embed",
     "mk_lm_head_parts", "mk_lm_head_argmax", "mk_launches_per_forward", "mk_lm_head_argmax_noalloc",
     "mk_topk_logprobs", "mk_forward_timed", "mk_sp_block", "mk_workspace_size_sp", "mk_forward_sp",
-    "mk_gemm_w8a16_fused",
+    "mk_gemm_w8a16_fused", "mk_set_sp_key_split",
 )
 
 MK_GEMM_ROWSCALE, MK_GEMM_RESID, MK_GEMM_SWIGLU, MK_GEMM_COLSCALE, MK_GEMM_RESID32 = 0, 1, 2, 3, 4
@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
         L.mk_sp_block.restype = _i32
         L.mk_sp_block.argtypes = [_vp, _i32, _i32]
         L.mk_workspace_size_sp.argtypes = [_vp, _i32, _i32, ctypes.POINTER(_sz)]
+        L.mk_set_sp_key_split.argtypes = [_vp, _i32]
         L.mk_forward_sp.argtypes = [_vp, _vp, _i32, _i32, _i32, ALLGATHER_FN, _vp, _vp, _sz, _vp, _vp, _vp, _vp,
                                     ctypes.POINTER(MkStageTimesC)]
         L.mk_get_error.argtypes = [_vp, ctypes.POINTER(_i32)]

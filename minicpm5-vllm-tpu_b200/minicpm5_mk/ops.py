@@ -118,6 +118,11 @@ class MkEngine:
     def sp_block(self, seq: int, world: int) -> int:
         return int(_lib.lib().mk_sp_block(self._h, seq, world))
 
+    def set_sp_key_split(self, enabled: bool) -> None:
+        """mk_set_sp_key_split: let forward_sp cut long causal key ranges over several attention CTAs (the
+        default); disabled, forward_sp is bit-identical to forward."""
+        _lib.check(_lib.lib().mk_set_sp_key_split(self._h, 1 if enabled else 0), "mk_set_sp_key_split")
+
     def sp_workspace(self, seq: int, world: int) -> torch.Tensor:
         """The workspace mk_forward_sp uses (shared with `forward`'s): bind the all-gather callback to it."""
         n = ctypes.c_size_t()

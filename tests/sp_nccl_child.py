@@ -1,5 +1,6 @@
 """One rank of the two-GPU sequence-parallel check (launched by tests/test_sp_gpu.py through
-torch.distributed.run): mk_forward_sp over NCCL must give rank 0 the same bits as mk_forward on one GPU."""
+torch.distributed.run): mk_forward_sp over NCCL (key split off) must give rank 0 the same bits as mk_forward
+on one GPU."""
 import os
 import sys
 from datetime import timedelta
@@ -21,6 +22,7 @@ def main():
 
     cfg = get_config("minicpm5-1b").replace(max_seq=8192)
     eng = MkEngine(cfg, mk_weights.prepare_mk_weights(random_state_dict(cfg, seed=1234, device=dev), cfg), dev)
+    eng.set_sp_key_split(False)  # one attention CTA per query block: the same bits as the one-GPU forward
     ids = synthetic_ids(1, 8192, seed=1234).reshape(-1).contiguous().to(dev)
     h1, l1, t1 = eng.forward_sp(ids, 8192, rank, world, sp.nccl_allgather())
     torch.cuda.synchronize()
