@@ -181,8 +181,9 @@ mk_status launch_k_pair(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
 // Tokens per GEMM tile for M tokens and N output channels on `sms` SMs.  The persistent GEMM runs
 // ceil(tiles / sms) waves of tiles; a tile of nt tokens costs about nt + 32 token-steps (the weight tile's
 // conversion and the epilogue's fixed work).  At large M every size fills its waves and the largest tile
-// wins; when all tiles fit in one or two waves (the projections of one sequence-parallel rank, an
-// isolated N = 1792 GEMM at M = 8192) smaller tiles finish sooner.  Candidates are multiples of 32: the
+// wins (ties go to the larger tile); when all tiles fit in one or two waves (the projections of one
+// sequence-parallel rank, an isolated N = 1792 GEMM at M = 8192) smaller tiles finish sooner: at 8 ranks
+// (1024 rows) o_proj and down take 96-token tiles.  Candidates are multiples of 32 from 192 down to 64: the
 // epilogue works in 32-token chunks, and with 32-aligned tiles no chunk straddles a sequence or zig-zag
 // block boundary, and every position's RoPE angle comes from the same table entry and the same number
 // of angle-addition steps whatever the batch size -- which keeps the forward batch-invariant bit for bit.
@@ -191,7 +192,7 @@ int choose_nt(int M, int N, int sms) {
   const int nc = N / mk::GW;
   int best = mk::GT;
   long best_cost = -1;
-  for (int nt = mk::GT; nt >= 128; nt -= 32) {
+  for (int nt = mk::GT; nt >= 64; nt -= 32) {
     const long tiles = static_cast<long>((M + nt - 1) / nt) * nc;
     const long cost = ((tiles + sms - 1) / sms) * (nt + 32);
     if (best_cost < 0 || cost < best_cost) {
