@@ -52,10 +52,14 @@ def _args():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--kernel", default=None,
                     choices=["gemm_swiglu", "gemm_qkv", "gemm_qkv_rope", "gemm_o", "gemm_kv", "gemm_down", "attn",
+                             "forward_sp",
                              "forward", "lm_head"],
                     help="time one isolated kernel of the forward, or whole forwards of --kernel-bs sequences "
                          "(profiling driver), instead of the bench")
     ap.add_argument("--kernel-bs", type=int, default=4, help="sequences of --seq tokens for --kernel")
+    ap.add_argument("--sp-world", type=int, default=8,
+                    help="--kernel forward_sp: rank 0 of this many sequence-parallel ranks on one GPU, the K/V "
+                         "all-gather replaced by copies of the rank's own rows (profiling driver)")
     ap.add_argument("--kernel-iters", type=int, default=3)
     ap.add_argument("--isolated", action="store_true",
                     help="time the isolated-kernel configuration (GEMMs at M=8192, attention at S=8192) and print "
@@ -238,6 +242,29 @@ def run_kernel(a):
         ids = synthetic_ids(a.kernel_bs, a.seq, seed=1234).reshape(-1).contiguous().to(dev)
         fn = lambda: eng.forward(ids, a.kernel_bs, a.seq)  # noqa: E731
         flops = _flops_per_seq(cfg, a.seq) * a.kernel_bs
+    elif a.kernel == "forward_sp":
+        # rank 0 of a --sp-world layout on this GPU alone: every kernel of the rank's forward runs at its real
+        # shape (the key-split attention included); the all-gather copies the rank's own K/V rows into every
+        # rank's slot, so no other GPU is needed (the numbers are not a sequence-parallel result)
+        from minicpm5_mk import mk_weights, sp
+        from minicpm5_mk.mk_init import random_state_dict, synthetic_ids
+        cfg = cfg.replace(max_seq=max(a.seq, cfg.max_seq))
+        sd = random_state_dict(cfg, seed=1234, device=dev)
+        eng = ops.MkEngine(cfg, mk_weights.prepare_mk_weights(sd, cfg), dev)
+        del sd
+        ids = synthetic_ids(1, a.seq, seed=1234).reshape(-1).contiguous().to(dev)
+        world = a.sp_world
+
+        def bind(ws):
+            def gather(send, recv, nbytes, s):
+                src, dst = sp._slice(ws, send, nbytes), sp._slice(ws, recv, nbytes * world)
+                for r in range(world):
+                    dst[r * nbytes:(r + 1) * nbytes].copy_(src)
+                return 0
+            return gather
+
+        fn = lambda: eng.forward_sp(ids, a.seq, 0, world, bind)  # noqa: E731
+        flops = _flops_per_seq(cfg, a.seq) / world
     elif a.kernel == "gemm_qkv_rope":
         # the forward's QKV projection: rstd from per-tile sums of squares, RoPE on the Q/K columns
         from minicpm5_mk.mk_weights import rope_tables
