@@ -306,6 +306,8 @@ def run_kernel(a):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.kernel_iters
     line = {"kernel": a.kernel, "tokens": T, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1)}
+    if a.kernel == "forward_sp":  # one sequence, this rank's share of it
+        line.update(tokens=a.seq, ranks=a.sp_world, rank_rows=a.seq // a.sp_world)
     if a.kernel == "lm_head":
         line["weight_gbs"] = round(cfg.vocab * cfg.hidden * 2 * -(-a.kernel_bs // 8) / ms / 1e6, 1)
     if a.kernel == "forward":  # per-stage device time of one more forward (events between the launches)
